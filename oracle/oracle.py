@@ -1,0 +1,169 @@
+"""ctypes binding of the CPU oracle (oracle.cpp) — TEST INFRASTRUCTURE ONLY.
+
+Loaded by the test suite, ``__graft_entry__.smoke()`` and the CPU-baseline leg
+of ``bench.py``; the product package never imports this module.  Every
+function mirrors one reference CPU operator (file:line cited in oracle.cpp).
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_SO = os.path.join(_HERE, "_build", "liboracle.so")
+_lib = None
+
+
+def build() -> str:
+    """Compile liboracle.so with the committed Makefile (idempotent)."""
+    subprocess.run(["make", "-s", "-C", _HERE], check=True)
+    return _SO
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        if not os.path.exists(_SO) or (
+                os.path.getmtime(_SO) < os.path.getmtime(os.path.join(_HERE, "oracle.cpp"))):
+            build()
+        L = ctypes.CDLL(_SO)
+        vp, sz, i32, f32 = ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int32, ctypes.c_float
+        L.oracle_dql.argtypes = [vp, sz, vp, vp, vp]
+        L.oracle_rowsum_u8.argtypes = [vp, sz, sz, vp]
+        L.oracle_matmul_integer.argtypes = [vp, ctypes.c_int, vp, ctypes.c_int, sz, sz, sz,
+                                            i32, vp, ctypes.c_int, vp, ctypes.c_int]
+        L.oracle_cast_i32_f32.argtypes = [vp, sz, vp]
+        L.oracle_mul_scalar_vec.argtypes = [f32, vp, sz, vp]
+        L.oracle_mul_rows.argtypes = [vp, sz, sz, vp, sz, vp]
+        L.oracle_add_bias.argtypes = [vp, sz, sz, vp, vp]
+        L.oracle_erf.argtypes = [vp, sz, vp]
+        L.oracle_gelu.argtypes = [vp, sz, vp]
+        L.oracle_dequantize_linear.argtypes = [vp, ctypes.c_int, sz, sz, sz, vp, sz, vp, vp]
+        L.oracle_quant_linear.argtypes = [vp, sz, sz, vp, sz, vp, ctypes.c_int, vp, ctypes.c_int,
+                                          vp, ctypes.c_int, vp, vp, vp, vp, vp, ctypes.c_int]
+        L.oracle_max_threads.restype = ctypes.c_int
+        _lib = L
+    return _lib
+
+
+def _p(a: np.ndarray | None):
+    return None if a is None else a.ctypes.data_as(ctypes.c_void_p)
+
+
+def dynamic_quantize_linear(x: np.ndarray):
+    """DynamicQuantizeLinear (dynamic_quantize_linear.rs:32-112) -> (y, scale, zp)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.empty(x.shape, dtype=np.uint8)
+    s = np.zeros(1, dtype=np.float32)
+    z = np.zeros(1, dtype=np.uint8)
+    lib().oracle_dql(_p(x), x.size, _p(y), _p(s), _p(z))
+    return y, np.float32(s[0]), np.uint8(z[0])
+
+
+def rowsum_u8(a: np.ndarray) -> np.ndarray:
+    a = np.ascontiguousarray(a, dtype=np.uint8)
+    M, K = a.shape
+    out = np.empty(M, dtype=np.int32)
+    lib().oracle_rowsum_u8(_p(a), M, K, _p(out))
+    return out
+
+
+def matmul_integer(a: np.ndarray, b: np.ndarray, a_zp=None, b_zp=None, threads: int = 1):
+    """MatMulInteger (matmul_integer.rs:52-179, 239-267).
+
+    a: u8/i8 [M, K] (rank 3 is flattened as the GPU arm does, layout.rs:1058-1090),
+    b: u8/i8 [K, N]; a_zp scalar; b_zp scalar or per-column [N] (spec extension).
+    """
+    lead = a.shape[:-1]
+    a2 = np.ascontiguousarray(a.reshape(-1, a.shape[-1]))
+    b = np.ascontiguousarray(b)
+    M, K = a2.shape
+    K2, N = b.shape
+    assert K == K2, "K mismatch"
+    out = np.empty((M, N), dtype=np.int32)
+    bz = None
+    per_col = 0
+    if b_zp is not None:
+        bz = np.ascontiguousarray(np.atleast_1d(np.asarray(b_zp)).astype(np.int32))
+        per_col = int(bz.size > 1)
+    az = 0 if a_zp is None else int(np.asarray(a_zp).reshape(-1)[0])
+    lib().oracle_matmul_integer(_p(a2), int(a2.dtype == np.int8), _p(b), int(b.dtype == np.int8),
+                                M, K, N, az, _p(bz), per_col, _p(out), threads)
+    return out.reshape(*lead, N)
+
+
+def cast_i32_f32(x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.int32)
+    y = np.empty(x.shape, dtype=np.float32)
+    lib().oracle_cast_i32_f32(_p(x), x.size, _p(y))
+    return y
+
+
+def erf(x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.empty_like(x)
+    lib().oracle_erf(_p(x), x.size, _p(y))
+    return y
+
+
+def gelu(x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.empty_like(x)
+    lib().oracle_gelu(_p(x), x.size, _p(y))
+    return y
+
+
+def dequantize_linear(x: np.ndarray, scale: np.ndarray, zp=None, axis: int = 1) -> np.ndarray:
+    """DequantizeLinear (dequantize_linear.rs:32-179)."""
+    x = np.ascontiguousarray(x)
+    scale = np.ascontiguousarray(np.asarray(scale, dtype=np.float32).reshape(-1))
+    code = {np.dtype(np.int8): 0, np.dtype(np.uint8): 1, np.dtype(np.int32): 2}[x.dtype]
+    if scale.size == 1:
+        outer, axis_len, inner = 1, 1, x.size
+    else:
+        ax = axis + x.ndim if axis < 0 else axis
+        outer = int(np.prod(x.shape[:ax]))
+        axis_len = x.shape[ax]
+        inner = int(np.prod(x.shape[ax + 1:]))
+    zpa = None if zp is None else np.ascontiguousarray(np.asarray(zp, dtype=x.dtype).reshape(-1))
+    y = np.empty(x.shape, dtype=np.float32)
+    if x.size == 0:
+        return y
+    lib().oracle_dequantize_linear(_p(x), code, outer, axis_len, inner, _p(scale), scale.size,
+                                   _p(zpa), _p(y))
+    return y
+
+
+def quant_linear(x: np.ndarray, w: np.ndarray, w_scale, bias: np.ndarray, b_zp=None,
+                 gelu: bool = False, threads: int = 1):
+    """The whole DQL -> MatMulInteger -> Cast -> Mul -> Add [-> GELU] chain.
+
+    Returns (out f32 [M, N], q u8 [M, K], scale f32, zp u8, acc i32 [M, N]).
+    """
+    x2 = np.ascontiguousarray(x.reshape(-1, x.shape[-1]), dtype=np.float32)
+    M, K = x2.shape
+    w = np.ascontiguousarray(w, dtype=np.int8)
+    N = w.shape[1]
+    ws = np.ascontiguousarray(np.atleast_1d(np.asarray(w_scale, dtype=np.float32)))
+    bias = np.ascontiguousarray(bias, dtype=np.float32)
+    bz = None
+    bz_pc = 0
+    if b_zp is not None:
+        bz = np.ascontiguousarray(np.atleast_1d(np.asarray(b_zp)).astype(np.int32))
+        bz_pc = int(bz.size > 1)
+    out = np.empty((M, N), dtype=np.float32)
+    q = np.empty((M, K), dtype=np.uint8)
+    s = np.zeros(1, dtype=np.float32)
+    z = np.zeros(1, dtype=np.uint8)
+    acc = np.empty((M, N), dtype=np.int32)
+    lib().oracle_quant_linear(_p(x2), M, K, _p(w), N, _p(ws), int(ws.size > 1), _p(bz), bz_pc,
+                              _p(bias), int(gelu), _p(out), _p(q), _p(s), _p(z), _p(acc), threads)
+    return out, q, np.float32(s[0]), np.uint8(z[0]), acc
+
+
+def max_threads() -> int:
+    return int(lib().oracle_max_threads())
