@@ -1,0 +1,445 @@
+"""Benchmark of the int8 dynamic-quantization hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload ffn|sweep]
+                    [--impl ours|reference]
+
+One JSON line on stdout (rank 0).  A "step" is one pass of the hot path over
+one batch of seeded synthetic input (no dataset or checkpoint exists here):
+
+* ``ffn``   (default): the int8 FFN block of the DistilBERT/BERT layer, batch
+  32 x seq 128 (M = 4096): DynamicQuantizeLinear -> MatMulInteger(768x3072)
+  -> dequant + bias -> erf-GELU -> DynamicQuantizeLinear ->
+  MatMulInteger(3072x768) -> dequant + bias.  Metric: sequences/s.
+* ``sweep``: one large-M point of the fused chain (M=65536, K=N=4096).
+
+Timing: W untimed warm-up steps, then K steps each bracketed by CUDA events
+on the launching stream, with a 256 MiB L2 flush between steps (outside the
+events); barrier + synchronize on both sides; max over ranks.  Multi-GPU runs
+shard the batch: every rank processes its own batch (weak scaling, no
+collective on the data path).  ``e2e`` times the same step through the public
+API from pinned host memory, including the H2D copy of the input and the D2H
+copy of the output.  ``roofline`` is measured for the fused GEMM kernel by
+CUDA events around back-to-back launches of that kernel.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "DistilBERT-int8 seq/s at 1/2/4/8 B200; MatMulInteger int8 TOPS vs peak"
+INT8_PEAK_TOPS = 4500.0  # B200 dense int8, datasheet (no measured int8 peak on this pool)
+
+
+def load_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return json.load(f), "measured"
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "fallback"
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------- workloads
+class FfnWorkload:
+    """Config 2: int8 FFN block, batch 32 x seq 128 (M=4096), K=768, F=3072."""
+
+    name = "ffn"
+
+    def __init__(self, device, batch=32, seq=128, hidden=768, ffn=3072, seed_base=0):
+        import torch
+        from iconnx_b200 import ops, synth
+        self.torch, self.ops = torch, ops
+        self.device = device
+        self.batch, self.seq, self.hidden, self.ffn = batch, seq, hidden, ffn
+        self.M = batch * seq
+        x = synth.normal((self.M, hidden), 1.0, seed_base + 0)
+        w1 = synth.int8_uniform((hidden, ffn), 1)
+        w2 = synth.int8_uniform((ffn, hidden), 3)
+        b1 = synth.normal((ffn,), 0.02, 2)
+        b2 = synth.normal((hidden,), 0.02, 102)
+        self.x_host = torch.from_numpy(x).pin_memory()
+        self.x = self.x_host.to(device)
+        self.w1 = ops.prepare_weight(torch.from_numpy(w1).to(device))
+        self.w2 = ops.prepare_weight(torch.from_numpy(w2).to(device))
+        self.b1 = torch.from_numpy(b1).to(device)
+        self.b2 = torch.from_numpy(b2).to(device)
+        self.ws = torch.tensor([0.01], dtype=torch.float32, device=device)
+        self.out_host = torch.empty((self.M, hidden), dtype=torch.float32).pin_memory()
+        self.units_per_step = batch  # sequences
+        self.unit = "seq/s"
+        self.launches_per_step = 6   # 2 x (minmax, quantize, fused GEMM)
+        self.gemm_ops = 2 * (2.0 * self.M * hidden * ffn)
+
+    def step(self, x=None):
+        ops = self.ops
+        h, *_ = ops.dynamic_quant_linear(self.x if x is None else x, self.w1, self.ws, self.b1,
+                                         gelu=True)
+        out, *_ = ops.dynamic_quant_linear(h, self.w2, self.ws, self.b2)
+        return out
+
+    def e2e_step(self):
+        torch = self.torch
+        x = self.x_host.to(self.device, non_blocking=True)
+        out = self.step(x)
+        self.out_host.copy_(out, non_blocking=True)
+        return int(self.x_host.numel() * 4), int(self.out_host.numel() * 4)
+
+    # dominant kernel: the GELU-fused GEMM1 (M x 768 x 3072)
+    def gemm_probe(self):
+        ops = self.ops
+        y, s, z = ops.gpu_dynamic_quantize_linear(self.x)
+        out = self.torch.empty((self.M, self.ffn), dtype=self.torch.float32, device=self.device)
+
+        def launch():
+            ops.quant_linear(y, s, z, self.w1, self.ws, self.b1, gelu=True, out=out)
+        M, K, N = self.M, self.hidden, self.ffn
+        ops_count = 2.0 * M * N * K
+        bytes_alg = M * K + N * K + 4 * M * N + 4 * N * 2
+        return launch, ops_count, bytes_alg, f"quant_linear_gelu M={M} K={K} N={N}"
+
+    def cpu_sample(self, threads):
+        """Oracle FFN block on ONE sequence (M=128)."""
+        from oracle import oracle
+        xs = self.x_host.numpy()[: self.seq]
+        w1 = self.w1_host if hasattr(self, "w1_host") else None
+        from iconnx_b200 import synth
+        w1 = synth.int8_uniform((self.hidden, self.ffn), 1)
+        w2 = synth.int8_uniform((self.ffn, self.hidden), 3)
+        b1 = synth.normal((self.ffn,), 0.02, 2)
+        b2 = synth.normal((self.hidden,), 0.02, 102)
+        ws = np.array([0.01], np.float32)
+        t0 = time.perf_counter()
+        h = oracle.quant_linear(xs, w1, ws, b1, None, True, threads=threads)[0]
+        oracle.quant_linear(h, w2, ws, b2, None, False, threads=threads)
+        dt = time.perf_counter() - t0
+        return 1.0 / dt, f"FFN block on 1 sequence (M={self.seq}) of the same workload"
+
+
+class SweepWorkload:
+    """Config 5 large-M point: DQL -> MatMulInteger -> dequant + bias."""
+
+    name = "sweep"
+
+    def __init__(self, device, M=65536, K=4096, N=4096, seed_base=0):
+        import torch
+        from iconnx_b200 import ops, synth
+        self.torch, self.ops, self.device = torch, ops, device
+        self.M, self.K, self.N = M, K, N
+        x = synth.outlier_mix((M, K), seed_base)
+        self.x_host = torch.from_numpy(x).pin_memory()
+        self.x = self.x_host.to(device)
+        self.w = ops.prepare_weight(torch.from_numpy(synth.int8_uniform((K, N), 1)).to(device))
+        self.bias = torch.from_numpy(synth.normal((N,), 0.02, 2)).to(device)
+        self.ws = torch.tensor([0.01], dtype=torch.float32, device=device)
+        self.out_host = torch.empty((M, N), dtype=torch.float32).pin_memory()
+        self.units_per_step = 2.0 * M * N * K / 1e12
+        self.unit = "TOPS"
+        self.launches_per_step = 3
+        self.gemm_ops = 2.0 * M * N * K
+
+    def step(self, x=None):
+        out, *_ = self.ops.dynamic_quant_linear(self.x if x is None else x, self.w, self.ws,
+                                                self.bias)
+        return out
+
+    def e2e_step(self):
+        x = self.x_host.to(self.device, non_blocking=True)
+        out = self.step(x)
+        self.out_host.copy_(out, non_blocking=True)
+        return int(self.x_host.numel() * 4), int(self.out_host.numel() * 4)
+
+    def gemm_probe(self):
+        ops = self.ops
+        y, s, z = ops.gpu_dynamic_quantize_linear(self.x)
+        out = self.torch.empty((self.M, self.N), dtype=self.torch.float32, device=self.device)
+
+        def launch():
+            ops.quant_linear(y, s, z, self.w, self.ws, self.bias, out=out)
+        M, K, N = self.M, self.K, self.N
+        return launch, 2.0 * M * N * K, M * K + N * K + 4 * M * N, f"quant_linear M={M} K={K} N={N}"
+
+    def cpu_sample(self, threads):
+        from oracle import oracle
+        m = 64
+        xs = self.x_host.numpy()[:m]
+        from iconnx_b200 import synth
+        w = synth.int8_uniform((self.K, self.N), 1)
+        b = synth.normal((self.N,), 0.02, 2)
+        t0 = time.perf_counter()
+        oracle.quant_linear(xs, w, np.array([0.01], np.float32), b, None, False, threads=threads)
+        dt = time.perf_counter() - t0
+        return 2.0 * m * self.N * self.K / dt / 1e12, f"fused chain on {m} rows of the same workload"
+
+
+WORKLOADS = {"ffn": FfnWorkload, "sweep": SweepWorkload}
+
+
+# ------------------------------------------------------------------ helpers
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def cpu_info():
+    model = ""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for ln in f:
+                if ln.startswith("model name"):
+                    model = ln.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    return os.cpu_count() or 1, model
+
+
+def run_reference(args):
+    """CPU implementation of the path (the oracle restating the reference's
+    single-threaded CPU operators), run with every host thread."""
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    from oracle import oracle
+    ncores, model = cpu_info()
+    threads = oracle.max_threads()
+
+    class _Host:  # CPU-only stand-in holding the same seeded inputs
+        pass
+
+    import torch
+    from iconnx_b200 import synth
+    if args.workload == "ffn":
+        w = FfnWorkload.__new__(FfnWorkload)
+        w.batch, w.seq, w.hidden, w.ffn = 32, 128, 768, 3072
+        w.x_host = torch.from_numpy(synth.normal((128, 768), 1.0, 0))
+        fn = lambda: FfnWorkload.cpu_sample(w, threads)  # noqa: E731
+        unit = "seq/s"
+        cfg = {"workload": "C2 int8 FFN block (batch 32 x seq 128, 768->3072->768)"}
+    else:
+        w = SweepWorkload.__new__(SweepWorkload)
+        w.M, w.K, w.N = 65536, 4096, 4096
+        w.x_host = torch.from_numpy(synth.outlier_mix((64, 4096), 0))
+        fn = lambda: SweepWorkload.cpu_sample(w, threads)  # noqa: E731
+        unit = "TOPS"
+        cfg = {"workload": "C5 fused chain M=65536 K=N=4096"}
+    for _ in range(args.warmup):
+        fn()
+    vals = []
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        v, sample = fn()
+        vals.append(v)
+    dt = time.perf_counter() - t0
+    value = float(np.mean(vals))
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": unit,
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "u8xs8->s32, f32 epilogue",
+            "data": "synthetic (seeded)", "config": cfg,
+            "cpu_baseline": {"value": value, "unit": unit, "cores": threads, "kind": "port",
+                             "sample": sample + f"; host: {ncores} cores, {model}"},
+            "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--workload", default="ffn", choices=sorted(WORKLOADS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    if args.impl == "reference":
+        run_reference(args)
+        return
+
+    import torch
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    pg = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=dev)
+        pg = dist
+    wl = WORKLOADS[args.workload](dev, seed_base=1000 * rank)
+    stream = torch.cuda.current_stream(dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def barrier():
+        if pg is not None:
+            pg.barrier()
+        torch.cuda.synchronize(dev)
+
+    # ---- device-resident timing (value)
+    g = torch.cuda.CUDAGraph()
+    for _ in range(2):
+        wl.step()
+    torch.cuda.synchronize(dev)
+    with torch.cuda.graph(g):
+        wl.step()
+    for _ in range(args.warmup):
+        g.replay()
+    barrier()
+    clocks = ClockSampler(local)
+    clocks.start()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
+    for s, e in evs:
+        flush.fill_(1)
+        s.record(stream)
+        g.replay()
+        e.record(stream)
+    barrier()
+    clk = clocks.stop()
+    step_ms = [s.elapsed_time(e) for s, e in evs]
+    total_ms = float(np.sum(step_ms))
+    t = torch.tensor([total_ms], device=dev)
+    if pg is not None:
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+    total_ms = float(t.item())
+    value = wl.units_per_step * world * args.steps / (total_ms / 1e3)
+
+    # ---- end-to-end through the public API, host buffers (e2e)
+    for _ in range(args.warmup):
+        wl.e2e_step()
+    barrier()
+    s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s_ev.record(stream)
+    for _ in range(args.steps):
+        h2d, d2h = wl.e2e_step()
+    e_ev.record(stream)
+    barrier()
+    e2e_ms = s_ev.elapsed_time(e_ev)
+    t = torch.tensor([e2e_ms], device=dev)
+    if pg is not None:
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+    e2e_ms = float(t.item())
+    e2e_value = wl.units_per_step * world * args.steps / (e2e_ms / 1e3)
+
+    # ---- roofline of the dominant kernel (fused GEMM), back-to-back launches
+    launch, ops_count, bytes_alg, kdesc = wl.gemm_probe()
+    reps = 20
+    for _ in range(3):
+        launch()
+    gk = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gk):
+        for _ in range(reps):
+            launch()
+    gk.replay()
+    torch.cuda.synchronize(dev)
+    ks, ke = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ks.record(stream)
+    gk.replay()
+    ke.record(stream)
+    torch.cuda.synchronize(dev)
+    k_ms = ks.elapsed_time(ke) / reps
+    peaks, peak_kind = load_peaks()
+    tops = ops_count / (k_ms / 1e3) / 1e12
+    gbs = bytes_alg / (k_ms / 1e3) / 1e9
+    t_tensor = ops_count / (INT8_PEAK_TOPS * 1e12)
+    t_hbm = bytes_alg / (peaks["hbm_gbs"] * 1e9)
+    if t_tensor >= t_hbm:
+        roof = {"bound": "tensor", "achieved": tops, "peak": INT8_PEAK_TOPS, "unit": "TOP/s",
+                "frac": tops / INT8_PEAK_TOPS, "peak_source": "datasheet dense int8 (no measured int8 peak)"}
+    else:
+        roof = {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": gbs / peaks["hbm_gbs"], "peak_source": f"{peak_kind} hbm_gbs"}
+    roof.update({"traffic": None, "kernel": kdesc, "kernel_ms": k_ms, "int8_tops": tops,
+                 "tensor_frac_of_4500": tops / INT8_PEAK_TOPS})
+
+    line = {"metric": METRIC, "value": value, "unit": wl.unit, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "u8xs8->s32, f32 epilogue", "data": "synthetic (seeded)",
+            "config": {"workload": wl.name, "M_per_gpu": wl.M,
+                       "l2": "256 MiB flush between timed steps", "parallelism": f"batch-shard x{world}"},
+            "e2e": {"value": e2e_value, "unit": wl.unit, "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+            "gpu_launches": wl.launches_per_step * args.steps,
+            "roofline": roof, "clocks": clk}
+    if wl.name == "ffn":
+        line["config"].update({"model": "DistilBERT-base FFN block (int8)", "global_batch": 32 * world,
+                               "seq_len": 128})
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle import oracle
+        ncores, model = cpu_info()
+        v, sample = wl.cpu_sample(1)
+        line["cpu_baseline"] = {"value": v, "unit": wl.unit, "cores": 1, "kind": "port",
+                                "sample": sample + f"; host {ncores} cores, {model}"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if pg is not None:
+        pg.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,276 @@
+// DynamicQuantizeLinear on the GPU, bit-exact with the reference CPU forward
+// (src/operators/dynamic_quantize_linear.rs:32-112).
+//
+// Two HBM-bound passes:
+//   1. dql_minmax_kernel: vectorised 16-byte loads, per-thread fminf/fmaxf
+//      seeded with 0 (fminf/fmaxf drop NaN exactly like the reference's
+//      `continue`), warp-shuffle then block reduction, one (min, max) pair
+//      per block written to the caller's workspace.  It also zeroes the
+//      optional row-sum output.
+//   2. dql_quantize_kernel: every block folds the partials (a few KB, L2
+//      resident), derives scale/zero-point in f64 exactly as the reference
+//      does, then quantises 16 elements per thread (four 16-byte loads, one
+//      16-byte store) and optionally accumulates per-row sums of y.
+//
+// Exactness of the per-element quantisation.  The reference computes
+// rte(f64(x) / scale) with an f64 division.  Here t = x * f32(1/scale) is
+// computed in f32; since |x / scale| <= 255, |t - x/scale| < 3.1e-5.  If t is
+// farther than 1e-4 from the nearest half-integer, rounding t and rounding
+// the exact quotient give the same integer, so rintf(t) is the reference's
+// result.  Otherwise (about 0.02% of random inputs, and all exact ties) the
+// element takes the f64 division path.  Non-finite values and scales whose
+// reciprocal is not a normal f32 also take the f64 path.
+#include "capi.cuh"
+#include "common.cuh"
+
+namespace icx {
+
+constexpr int kMinmaxThreads = 512;
+constexpr int kQuantThreads = 256;
+constexpr int kMaxPartials = 148 * 8;
+
+__device__ __forceinline__ void warp_minmax(float& mn, float& mx) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  }
+}
+
+// Block-wide (min, max) reduction; result valid in thread 0.
+template <int THREADS>
+__device__ __forceinline__ void block_minmax(float& mn, float& mx) {
+  __shared__ float s_mn[THREADS / 32], s_mx[THREADS / 32];
+  warp_minmax(mn, mx);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  if (l == 0) {
+    s_mn[w] = mn;
+    s_mx[w] = mx;
+  }
+  __syncthreads();
+  if (w == 0) {
+    mn = l < THREADS / 32 ? s_mn[l] : 0.0f;
+    mx = l < THREADS / 32 ? s_mx[l] : 0.0f;
+    warp_minmax(mn, mx);
+  }
+}
+
+__global__ void __launch_bounds__(kMinmaxThreads)
+    dql_minmax_kernel(const float* __restrict__ x, size_t n,
+                      float2* __restrict__ partials,
+                      int32_t* __restrict__ rowsum, size_t nrows) {
+  float mn = 0.0f, mx = 0.0f;  // the reference seeds the scan with 0.0
+  const size_t tid = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const size_t stride = (size_t)gridDim.x * blockDim.x;
+  size_t head = n;
+  if ((reinterpret_cast<uintptr_t>(x) & 15) == 0) {
+    const float4* x4 = reinterpret_cast<const float4*>(x);
+    const size_t n4 = n / 4;
+    size_t i = tid;
+    // four independent 16-byte loads in flight per thread
+    for (; i + 3 * stride < n4; i += 4 * stride) {
+      float4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) v[u] = __ldg(x4 + i + u * stride);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        mn = fminf(fminf(mn, v[u].x), fminf(v[u].y, fminf(v[u].z, v[u].w)));
+        mx = fmaxf(fmaxf(mx, v[u].x), fmaxf(v[u].y, fmaxf(v[u].z, v[u].w)));
+      }
+    }
+    for (; i < n4; i += stride) {
+      float4 v = __ldg(x4 + i);
+      mn = fminf(fminf(mn, v.x), fminf(v.y, fminf(v.z, v.w)));
+      mx = fmaxf(fmaxf(mx, v.x), fmaxf(v.y, fmaxf(v.z, v.w)));
+    }
+    head = n4 * 4;
+  } else {
+    head = 0;
+  }
+  for (size_t i = head + tid; i < n; i += stride) {
+    float v = __ldg(x + i);
+    mn = fminf(mn, v);
+    mx = fmaxf(mx, v);
+  }
+  block_minmax<kMinmaxThreads>(mn, mx);
+  if (threadIdx.x == 0) partials[blockIdx.x] = make_float2(mn, mx);
+  if (rowsum != nullptr)
+    for (size_t r = tid; r < nrows; r += stride) rowsum[r] = 0;
+}
+
+struct DqlParams {
+  double scale;   // f64 scale (0 when min == max)
+  float inv32;    // f32(1 / scale) for the fast path
+  float zpf;      // zero point as float
+  int fast;       // inv32 usable
+  int zero;       // min == max: everything quantises to 0
+};
+
+// scale / zero point exactly as dynamic_quantize_linear.rs:75-92.
+__device__ __forceinline__ DqlParams dql_params(float fmn, float fmx) {
+  DqlParams p;
+  const double mn = (double)fmn, mx = (double)fmx;
+  if (mn == mx) {
+    p.scale = 0.0;
+    p.inv32 = 0.0f;
+    p.zpf = 0.0f;
+    p.fast = 0;
+    p.zero = 1;
+    return p;
+  }
+  p.zero = 0;
+  p.scale = (mx - mn) / 255.0;
+  double izp = rint(0.0 - mn / p.scale);
+  izp = izp < 0.0 ? 0.0 : (izp > 255.0 ? 255.0 : izp);  // NaN handled below
+  if (isnan(izp)) izp = 0.0;
+  p.zpf = (float)izp;
+  const double inv = 1.0 / p.scale;
+  p.inv32 = (float)inv;
+  p.fast = (isfinite(p.scale) && inv >= 1.2e-38 && inv <= 3.0e38) ? 1 : 0;
+  return p;
+}
+
+__device__ __forceinline__ uint32_t quant1(float xv, const DqlParams& p) {
+  if (p.zero) return 0u;
+  if (p.fast) {
+    const float t = xv * p.inv32;
+    const float r = rintf(t);
+    const float f = fabsf(t - r);
+    if (fabsf(f - 0.5f) > 1e-4f) {
+      const float q = r + p.zpf;
+      return q > 0.0f ? (q < 255.0f ? (uint32_t)q : 255u) : 0u;
+    }
+  }
+  // f64 division path (ties, near-ties, non-finite inputs, extreme scales)
+  const double q = rint((double)xv / p.scale) + (double)p.zpf;
+  return q > 0.0 ? (q < 255.0 ? (uint32_t)q : 255u) : 0u;  // NaN -> 0
+}
+
+__device__ __forceinline__ uint32_t quant4(float4 v, const DqlParams& p,
+                                           uint32_t& sum) {
+  const uint32_t a = quant1(v.x, p), b = quant1(v.y, p), c = quant1(v.z, p),
+                 d = quant1(v.w, p);
+  sum += a + b + c + d;
+  return a | (b << 8) | (c << 16) | (d << 24);
+}
+
+__global__ void __launch_bounds__(kQuantThreads)
+    dql_quantize_kernel(const float* __restrict__ x, size_t n,
+                        const float2* __restrict__ partials, int nparts,
+                        uint8_t* __restrict__ y, float* __restrict__ scale_out,
+                        uint8_t* __restrict__ zp_out,
+                        int32_t* __restrict__ rowsum, size_t row_len,
+                        int vec16) {
+  __shared__ DqlParams s_p;
+  {
+    float mn = 0.0f, mx = 0.0f;
+    for (int i = threadIdx.x; i < nparts; i += kQuantThreads) {
+      const float2 v = partials[i];
+      mn = fminf(mn, v.x);
+      mx = fmaxf(mx, v.y);
+    }
+    block_minmax<kQuantThreads>(mn, mx);
+    if (threadIdx.x == 0) {
+      s_p = dql_params(mn, mx);
+      if (blockIdx.x == 0) {
+        *scale_out = (float)s_p.scale;
+        *zp_out = (uint8_t)s_p.zpf;
+      }
+    }
+    __syncthreads();
+  }
+  const DqlParams p = s_p;
+  const int lane = threadIdx.x & 31;
+  const size_t warp_g = ((size_t)blockIdx.x * kQuantThreads + threadIdx.x) >> 5;
+  const size_t nwarps = ((size_t)gridDim.x * kQuantThreads) >> 5;
+
+  size_t done = 0;
+  if (vec16) {
+    // 16 elements per thread; a chunk never straddles a row because the
+    // host only selects this path when row_len % 16 == 0 (or no row sums).
+    const size_t nchunks = n / 16;
+    const float4* x4 = reinterpret_cast<const float4*>(x);
+    uint4* y16 = reinterpret_cast<uint4*>(y);
+    for (size_t base = warp_g * 32; base < nchunks; base += nwarps * 32) {
+      const size_t c = base + lane;
+      const bool valid = c < nchunks;
+      uint32_t sum = 0;
+      if (valid) {
+        float4 v0 = __ldg(x4 + 4 * c), v1 = __ldg(x4 + 4 * c + 1),
+               v2 = __ldg(x4 + 4 * c + 2), v3 = __ldg(x4 + 4 * c + 3);
+        uint4 o;
+        o.x = quant4(v0, p, sum);
+        o.y = quant4(v1, p, sum);
+        o.z = quant4(v2, p, sum);
+        o.w = quant4(v3, p, sum);
+        y16[c] = o;
+      }
+      if (rowsum != nullptr) {
+        const unsigned long long row =
+            valid ? (unsigned long long)(c * 16 / row_len) : ~0ull;
+        const unsigned mask = __match_any_sync(0xffffffffu, row);
+        const uint32_t tot = __reduce_add_sync(mask, sum);
+        if (valid && lane == __ffs(mask) - 1)
+          atomicAdd(rowsum + row, (int32_t)tot);
+      }
+    }
+    done = nchunks * 16;
+  }
+  // scalar path: misaligned buffers, rows not a multiple of 16, and tails
+  const size_t tid = (size_t)blockIdx.x * kQuantThreads + threadIdx.x;
+  const size_t stride = (size_t)gridDim.x * kQuantThreads;
+  for (size_t i = done + tid; i < n; i += stride) {
+    const uint32_t q = quant1(__ldg(x + i), p);
+    y[i] = (uint8_t)q;
+    if (rowsum != nullptr && q != 0) atomicAdd(rowsum + i / row_len, (int32_t)q);
+  }
+}
+
+static int minmax_blocks(size_t n) {
+  size_t per_block = (size_t)kMinmaxThreads * 16;
+  size_t b = (n + per_block - 1) / per_block;
+  if (b < 1) b = 1;
+  if (b > (size_t)kMaxPartials) b = kMaxPartials;
+  return (int)b;
+}
+
+}  // namespace icx
+
+using namespace icx;
+
+extern "C" size_t icx_dql_workspace_bytes(size_t n) {
+  return (size_t)minmax_blocks(n) * sizeof(float2);
+}
+
+extern "C" int icx_dql_f32_u8(void* stream, const float* d_x, size_t n,
+                              uint8_t* d_y, float* d_scale, uint8_t* d_zp,
+                              int32_t* d_rowsum, size_t row_len,
+                              void* d_workspace, size_t workspace_bytes) {
+  ICX_REQUIRE(d_scale && d_zp, "DynamicQuantizeLinear: null scale/zp output");
+  ICX_REQUIRE(n == 0 || (d_x && d_y), "DynamicQuantizeLinear: null x or y");
+  ICX_REQUIRE(d_rowsum == nullptr || (row_len > 0 && n % row_len == 0),
+              "DynamicQuantizeLinear: row_len %zu must divide n %zu", row_len,
+              n);
+  const int blocks = minmax_blocks(n);
+  ICX_REQUIRE(d_workspace != nullptr &&
+                  workspace_bytes >= (size_t)blocks * sizeof(float2),
+              "DynamicQuantizeLinear: workspace %zu bytes < %zu required",
+              workspace_bytes, (size_t)blocks * sizeof(float2));
+  cudaStream_t s = as_stream(stream);
+  const size_t nrows = d_rowsum ? n / row_len : 0;
+  dql_minmax_kernel<<<blocks, kMinmaxThreads, 0, s>>>(
+      d_x, n, static_cast<float2*>(d_workspace), d_rowsum, nrows);
+  ICX_LAUNCH_CHECK();
+  const bool aligned = ((reinterpret_cast<uintptr_t>(d_x) |
+                         reinterpret_cast<uintptr_t>(d_y)) & 15) == 0;
+  const int vec16 = aligned && (d_rowsum == nullptr || row_len % 16 == 0);
+  size_t work = vec16 ? n / 16 : n;
+  size_t qb = (work + kQuantThreads - 1) / kQuantThreads;
+  if (qb < 1) qb = 1;
+  if (qb > 148 * 8) qb = 148 * 8;
+  dql_quantize_kernel<<<(int)qb, kQuantThreads, 0, s>>>(
+      d_x, n, static_cast<const float2*>(d_workspace), blocks, d_y, d_scale,
+      d_zp, d_rowsum, row_len ? row_len : 1, vec16);
+  ICX_LAUNCH_CHECK();
+  return ICX_OK;
+}

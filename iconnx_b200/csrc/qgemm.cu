@@ -1,0 +1,614 @@
+// MatMulInteger on the 5th-generation tensor cores (tcgen05.mma kind::i8),
+// with the zero-point correction and the Cast -> Mul -> Add [-> GELU]
+// epilogue fused, so the s32 accumulator stays in tensor memory.
+//
+// Replaces the reference's one-thread-per-output SIMT kernel
+// matmul_integer_u8s8_kernel (src/cuda/ops/quantize_kernels.rs:116-194) and
+// the Cast/Mul/Add/Erf launches that follow it (SURVEY call stack 3.2).
+//
+// Kernel structure (one CTA per SM, persistent over output tiles):
+//   warp 0      TMA producer: 128x128-byte A tiles and BNx128-byte B tiles
+//               (both K-major, 128-byte swizzle) into an S-stage ring.
+//   warp 1      owns the tensor-memory allocation; one elected thread issues
+//               tcgen05.mma (M=128, N=BN, K=32 per instruction) into one of
+//               two BN-column accumulators, so the epilogue of tile i
+//               overlaps the main loop of tile i+1.
+//   warps 2..5  epilogue: tcgen05.ld 32x32b.x32 (each warp owns the 32 TMEM
+//               lanes of its quadrant), zero-point correction in s32,
+//               f32 dequantisation, bias, optional GELU, global stores.
+// All mbarrier waits are bounded (common.cuh).
+//
+// Zero-point correction (exact modulo 2^32, like the reference's i32 math):
+//   sum_k (a - za)(b - zb[n]) = sum_k a*b - za*colsum_b[n] - zb[n]*rowsum_a[m]
+//                               + K*za*zb[n]
+// The tensor cores compute sum_k a*b on the raw u8/s8 values.
+#include <cuda.h>
+
+#include <mutex>
+#include <unordered_map>
+
+#include "capi.cuh"
+#include "common.cuh"
+
+namespace icx {
+
+constexpr int kBM = 128;      // rows per tile (UMMA M)
+constexpr int kBK = 128;      // K bytes per stage (one 128-byte swizzle atom)
+constexpr int kUmmaK = 32;    // K per tcgen05.mma kind::i8
+constexpr int kThreads = 192; // 6 warps
+constexpr int kEpiThreads = 128;
+
+enum EpiMode { kEpiS32 = 0, kEpiF32 = 1, kEpiGelu = 2 };
+
+struct GemmArgs {
+  int M, N, K;
+  const void* a_zp;     // nullable, 1 element of A's type
+  int a_zp_signed;
+  const void* b_zp;     // nullable, 1 or N elements of B's type
+  int b_zp_signed;
+  int b_zp_per_col;
+  const int32_t* colsum;  // [N], sum_k b[k, n]
+  const int32_t* rowsum;  // [M], sum_k a[m, k]; needed when b_zp != null
+  const float* a_scale;   // device scalar
+  const float* w_scale;   // 1 or N
+  int w_scale_per_col;
+  const float* bias;      // nullable, N
+  void* out;              // s32 or f32 [M, N]
+};
+
+template <int BN>
+struct Cfg {
+  static constexpr int kStages = BN == 256 ? 4 : 6;
+  static constexpr int kABytes = kBM * kBK;
+  static constexpr int kBBytes = BN * kBK;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kTmemCols = 2 * BN;
+  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ +
+                                    256 /*barriers*/ + 4 * BN * 4 /*params*/;
+};
+
+__device__ __forceinline__ int32_t ld_zp(const void* p, int is_signed,
+                                         int idx) {
+  return is_signed ? (int32_t)(static_cast<const int8_t*>(p)[idx])
+                   : (int32_t)(static_cast<const uint8_t*>(p)[idx]);
+}
+
+// Erf-GELU 0.5*x*(1+erf(x/sqrt2)) with the Abramowitz & Stegun 7.1.26 erf
+// the reference uses (src/operators/erf.rs:30-40), evaluated with fused
+// multiply-adds and the hardware exp2: within ~1e-6 absolute of the
+// reference's op-by-op f32 evaluation (tested bound 1e-5).
+__device__ __forceinline__ float gelu_erf(float x) {
+  const float d = x * 0.70710678118654752f;
+  const float a = fabsf(d);
+  const float t = __frcp_rn(fmaf(0.3275911f, a, 1.0f));
+  float p = fmaf(1.0614054f, t, -1.4531521f);
+  p = fmaf(p, t, 1.4214138f);
+  p = fmaf(p, t, -0.28449672f);
+  p = fmaf(p, t, 0.2548296f);
+  p = p * t;
+  const float e = __expf(-a * a);
+  const float erf_abs = fmaf(-p, e, 1.0f);
+  const float erf_v = copysignf(erf_abs, d);
+  return (x * (1.0f + erf_v)) * 0.5f;
+}
+
+// Named barrier among the 4 epilogue warps only.
+__device__ __forceinline__ void epi_sync() {
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+}
+
+template <int BN, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    qgemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA,
+                         const __grid_constant__ CUtensorMap tmB,
+                         const GemmArgs args, uint32_t idesc) {
+  using C = Cfg<BN>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + C::kStages * C::kABytes;
+  uint64_t* bars =
+      reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStageBytes);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + C::kStages;
+  uint64_t* tfull = bars + 2 * C::kStages;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  int32_t* s_corr = reinterpret_cast<int32_t*>(smem + C::kStages * C::kStageBytes + 256);
+  int32_t* s_bz = s_corr + BN;
+  float* s_scale = reinterpret_cast<float*>(s_bz + BN);
+  float* s_bias = s_scale + BN;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int M = args.M, N = args.N, K = args.K;
+  const int num_n = (N + BN - 1) / BN;
+  const int num_m = (M + kBM - 1) / kBM;
+  const int ntiles = num_m * num_n;
+  const int nk = (K + kBK - 1) / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 4);
+    }
+    fence_barrier_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------- producer
+    if (elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+        const int m0 = (t / num_n) * kBM;
+        const int n0 = (t % num_n) * BN;
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, ICX_DEVICE_TIMEOUT_PRODUCER)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], C::kStageBytes);
+          tma_load_2d(sA + stage * C::kABytes, &tmA, &full[stage], kb * kBK, m0);
+          tma_load_2d(sB + stage * C::kBBytes, &tmB, &full[stage], kb * kBK, n0);
+          if (++stage == C::kStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // --------------------------------------------------------- MMA issuer
+    if (elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, ICX_DEVICE_TIMEOUT_MMA)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait(&full[stage], phase, ICX_DEVICE_TIMEOUT_MMA)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t da = smem_desc_k128(smem_addr(sA + stage * C::kABytes));
+          const uint64_t db = smem_desc_k128(smem_addr(sB + stage * C::kBBytes));
+#pragma unroll
+          for (int k = 0; k < kBK / kUmmaK; ++k) {
+            // advance the start address by 32 bytes (encoded >> 4) per step
+            mma_i8(d_tmem, da + (uint64_t)(k * 2), db + (uint64_t)(k * 2), idesc,
+                   (kb | k) != 0);
+          }
+          mma_commit(&empty[stage]);
+          if (++stage == C::kStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        mma_commit(&tfull[acc]);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1;
+      }
+    }
+  } else {
+    // ----------------------------------------------------------- epilogue
+    const int quad = warp & 3;             // TMEM lanes [32*quad, 32*quad+32)
+    const int et = threadIdx.x - 64;       // 0..127
+    const int row_in_tile = quad * 32 + lane;
+    int32_t za = 0;
+    float a_scale = 0.0f;
+    if (args.a_zp) za = ld_zp(args.a_zp, args.a_zp_signed, 0);
+    if (EPI != kEpiS32) a_scale = *args.a_scale;
+    const bool has_bz = args.b_zp != nullptr;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    bool ok = true;  // false once a bounded wait gave up: skip work, keep barriers matched
+    for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
+      const int m0 = (t / num_n) * kBM;
+      const int n0 = (t % num_n) * BN;
+      // per-column constants of this tile
+      for (int j = et; j < BN; j += kEpiThreads) {
+        const int n = n0 + j;
+        int32_t cs = 0, bz = 0;
+        float sc = 0.0f, bi = 0.0f;
+        if (n < N) {
+          cs = args.colsum[n];
+          if (has_bz) bz = ld_zp(args.b_zp, args.b_zp_signed, args.b_zp_per_col ? n : 0);
+          if (EPI != kEpiS32) {
+            sc = __fmul_rn(a_scale, args.w_scale[args.w_scale_per_col ? n : 0]);
+            bi = args.bias ? args.bias[n] : 0.0f;
+          }
+        }
+        s_corr[j] = (int32_t)((uint32_t)K * (uint32_t)za * (uint32_t)bz -
+                              (uint32_t)za * (uint32_t)cs);
+        s_bz[j] = bz;
+        s_scale[j] = sc;
+        s_bias[j] = bi;
+      }
+      epi_sync();
+      const int m = m0 + row_in_tile;
+      const int32_t rs = (has_bz && m < M) ? args.rowsum[m] : 0;
+      if (ok) ok = mbar_wait(&tfull[acc], acc_phase, ICX_DEVICE_TIMEOUT_EPILOGUE);
+      tc_fence_after();
+      const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
+#pragma unroll 1
+      for (int c = 0; c < BN / 32 && ok; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(t_row + (uint32_t)(c * 32), r);
+        tmem_ld_wait();
+        const int nb = n0 + c * 32;
+        if (m < M && nb < N) {
+          const bool full_chunk = (nb + 32 <= N) && ((N & 3) == 0);
+          if (EPI == kEpiS32) {
+            int32_t* orow = static_cast<int32_t*>(args.out) + (size_t)m * N + nb;
+            int32_t v[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              v[j] = (int32_t)(r[j] + (uint32_t)s_corr[c * 32 + j] -
+                               (uint32_t)s_bz[c * 32 + j] * (uint32_t)rs);
+            if (full_chunk) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 4)
+                *reinterpret_cast<int4*>(orow + j) = make_int4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (nb + j < N) orow[j] = v[j];
+            }
+          } else {
+            float* orow = static_cast<float*>(args.out) + (size_t)m * N + nb;
+            float v[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const int32_t iv = (int32_t)(r[j] + (uint32_t)s_corr[c * 32 + j] -
+                                           (uint32_t)s_bz[c * 32 + j] * (uint32_t)rs);
+              float f = __fmul_rn(__int2float_rn(iv), s_scale[c * 32 + j]);
+              if (args.bias) f = __fadd_rn(f, s_bias[c * 32 + j]);
+              if (EPI == kEpiGelu) f = gelu_erf(f);
+              v[j] = f;
+            }
+            if (full_chunk) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 4)
+                *reinterpret_cast<float4*>(orow + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (nb + j < N) orow[j] = v[j];
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+      epi_sync();  // s_* params are rewritten for the next tile
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::kTmemCols);
+  }
+}
+
+// SIMT kernel for shapes the TMA path cannot address (K not a multiple of 16
+// or misaligned operands).  One thread per output; same arithmetic.
+template <int EPI>
+__global__ void qgemm_simt_kernel(const void* __restrict__ a, int a_signed,
+                                  const void* __restrict__ bt, int b_signed,
+                                  const GemmArgs args) {
+  const size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int M = args.M, N = args.N, K = args.K;
+  if (idx >= (size_t)M * N) return;
+  const int m = (int)(idx / N), n = (int)(idx % N);
+  uint32_t acc = 0;
+  for (int k = 0; k < K; ++k) {
+    const int32_t av = a_signed ? (int32_t)static_cast<const int8_t*>(a)[(size_t)m * K + k]
+                                : (int32_t)static_cast<const uint8_t*>(a)[(size_t)m * K + k];
+    const int32_t bv = b_signed ? (int32_t)static_cast<const int8_t*>(bt)[(size_t)n * K + k]
+                                : (int32_t)static_cast<const uint8_t*>(bt)[(size_t)n * K + k];
+    acc += (uint32_t)(av * bv);
+  }
+  const int32_t za = args.a_zp ? ld_zp(args.a_zp, args.a_zp_signed, 0) : 0;
+  const int32_t bz = args.b_zp ? ld_zp(args.b_zp, args.b_zp_signed, args.b_zp_per_col ? n : 0) : 0;
+  const int32_t rs = args.b_zp ? args.rowsum[m] : 0;
+  const int32_t v = (int32_t)(acc + (uint32_t)K * (uint32_t)za * (uint32_t)bz -
+                              (uint32_t)za * (uint32_t)args.colsum[n] -
+                              (uint32_t)bz * (uint32_t)rs);
+  if (EPI == kEpiS32) {
+    static_cast<int32_t*>(args.out)[idx] = v;
+  } else {
+    const float sc = __fmul_rn(*args.a_scale, args.w_scale[args.w_scale_per_col ? n : 0]);
+    float f = __fmul_rn(__int2float_rn(v), sc);
+    if (args.bias) f = __fadd_rn(f, args.bias[n]);
+    if (EPI == kEpiGelu) f = gelu_erf(f);
+    static_cast<float*>(args.out)[idx] = f;
+  }
+}
+
+// ---------------------------------------------------------------- host side
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
+                                  void*, const cuuint64_t*, const cuuint64_t*,
+                                  const cuuint32_t*, const cuuint32_t*,
+                                  CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion,
+                                  CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000,
+                                         cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// K-major byte matrix [rows, K] -> tensor map with a box of box_rows x 128
+// bytes and the 128-byte swizzle.  Out-of-range rows/columns read as zero.
+static int make_tmap(CUtensorMap* map, const void* base, size_t rows, size_t K,
+                     int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) {
+    set_error("cuTensorMapEncodeTiled unavailable from the driver");
+    return ICX_ERR_CUDA;
+  }
+  cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)K};
+  cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base),
+                  dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled failed (%d) rows=%zu K=%zu", (int)r, rows, K);
+    return ICX_ERR_CUDA;
+  }
+  return ICX_OK;
+}
+
+static int sm_count() {
+  int dev = 0, n = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
+template <int BN, int EPI>
+static int launch_tc(cudaStream_t s, const void* a, bool a_signed, const void* bt,
+                     bool b_signed, const GemmArgs& args) {
+  using C = Cfg<BN>;
+  CUtensorMap ta, tb;
+  int rc = make_tmap(&ta, a, (size_t)args.M, (size_t)args.K, kBM);
+  if (rc) return rc;
+  rc = make_tmap(&tb, bt, (size_t)args.N, (size_t)args.K, BN);
+  if (rc) return rc;
+  auto kern = qgemm_tcgen05_kernel<BN, EPI>;
+  ICX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                C::kSmemBytes));
+  const int ntiles = ((args.M + kBM - 1) / kBM) * ((args.N + BN - 1) / BN);
+  int grid = sm_count();
+  if (ntiles < grid) grid = ntiles;
+  const uint32_t idesc = idesc_i8(kBM, BN, a_signed, b_signed);
+  kern<<<grid, kThreads, C::kSmemBytes, s>>>(ta, tb, args, idesc);
+  ICX_LAUNCH_CHECK();
+  return ICX_OK;
+}
+
+template <int EPI>
+static int launch_gemm(cudaStream_t s, const void* a, bool a_signed,
+                       const void* bt, bool b_signed, const GemmArgs& args) {
+  if (args.M == 0 || args.N == 0) return ICX_OK;
+  const bool tma_ok = (args.K % 16 == 0) && args.K > 0 &&
+                      ((reinterpret_cast<uintptr_t>(a) |
+                        reinterpret_cast<uintptr_t>(bt)) & 15) == 0;
+  if (tma_ok) {
+    // narrow tiles when the wide ones would leave most SMs idle
+    const long tiles256 = (long)((args.M + kBM - 1) / kBM) * ((args.N + 255) / 256);
+    if (tiles256 >= sm_count() || args.N <= 128)
+      return args.N <= 128 ? launch_tc<128, EPI>(s, a, a_signed, bt, b_signed, args)
+                           : launch_tc<256, EPI>(s, a, a_signed, bt, b_signed, args);
+    return launch_tc<128, EPI>(s, a, a_signed, bt, b_signed, args);
+  }
+  const size_t total = (size_t)args.M * args.N;
+  const int threads = 256;
+  const size_t blocks = (total + threads - 1) / threads;
+  qgemm_simt_kernel<EPI><<<(unsigned)blocks, threads, 0, s>>>(a, a_signed, bt, b_signed, args);
+  ICX_LAUNCH_CHECK();
+  return ICX_OK;
+}
+
+// ------------------------------------------------------- weight preparation
+// bt[n, k] = b[k, n] through a 32x32 shared tile; colsum via atomics of
+// per-tile partial column sums.
+__global__ void prepare_b_kernel(const uint8_t* __restrict__ b, int b_signed,
+                                 int K, int N, uint8_t* __restrict__ bt,
+                                 int32_t* __restrict__ colsum) {
+  __shared__ uint8_t tile[32][33];
+  const int k0 = blockIdx.y * 32, n0 = blockIdx.x * 32;
+  const int tx = threadIdx.x, ty = threadIdx.y;  // 32 x 8
+  for (int i = ty; i < 32; i += 8) {
+    const int k = k0 + i, n = n0 + tx;
+    tile[i][tx] = (k < K && n < N) ? b[(size_t)k * N + n] : 0;
+  }
+  __syncthreads();
+  for (int i = ty; i < 32; i += 8) {
+    const int n = n0 + i, k = k0 + tx;
+    if (n < N && k < K) bt[(size_t)n * K + k] = tile[tx][i];
+  }
+  if (ty == 0 && n0 + tx < N) {
+    int32_t s = 0;
+    for (int i = 0; i < 32; ++i)
+      s += b_signed ? (int32_t)(int8_t)tile[i][tx] : (int32_t)tile[i][tx];
+    atomicAdd(colsum + n0 + tx, s);
+  }
+}
+
+// rowsum[m] = sum_k a[m, k] (one warp per row)
+__global__ void rowsum_kernel(const uint8_t* __restrict__ a, int a_signed,
+                              int M, int K, int32_t* __restrict__ rowsum) {
+  const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (w >= M) return;
+  int32_t s = 0;
+  for (int k = lane; k < K; k += 32) {
+    const uint8_t v = a[(size_t)w * K + k];
+    s += a_signed ? (int32_t)(int8_t)v : (int32_t)v;
+  }
+  for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if (lane == 0) rowsum[w] = s;
+}
+
+static bool is_8bit(int t) { return t == ICX_U8 || t == ICX_S8; }
+
+}  // namespace icx
+
+using namespace icx;
+
+extern "C" int icx_prepare_b(void* stream, const void* d_b, int b_type, size_t K,
+                             size_t N, void* d_bt, int32_t* d_colsum) {
+  ICX_REQUIRE(is_8bit(b_type), "MatMulInteger: b must be Int8 or UInt8");
+  ICX_REQUIRE(K < (1u << 30) && N < (1u << 30), "MatMulInteger: b too large");
+  if (K == 0 || N == 0) {
+    if (N && d_colsum) ICX_CUDA(cudaMemsetAsync(d_colsum, 0, N * 4, as_stream(stream)));
+    return ICX_OK;
+  }
+  ICX_REQUIRE(d_b && d_bt && d_colsum, "MatMulInteger: null weight buffer");
+  cudaStream_t s = as_stream(stream);
+  ICX_CUDA(cudaMemsetAsync(d_colsum, 0, N * sizeof(int32_t), s));
+  dim3 grid((unsigned)((N + 31) / 32), (unsigned)((K + 31) / 32));
+  prepare_b_kernel<<<grid, dim3(32, 8), 0, s>>>(
+      static_cast<const uint8_t*>(d_b), b_type == ICX_S8, (int)K, (int)N,
+      static_cast<uint8_t*>(d_bt), d_colsum);
+  ICX_LAUNCH_CHECK();
+  return ICX_OK;
+}
+
+static size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+extern "C" size_t icx_matmul_integer_workspace_bytes(size_t M, size_t K, size_t N) {
+  return align256(N * K) + align256(N * 4) + align256(M * 4);
+}
+
+extern "C" int icx_matmul_integer_prepared(
+    void* stream, const void* d_a, int a_type, const void* d_bt, int b_type,
+    const int32_t* d_colsum, size_t M, size_t K, size_t N, const void* d_a_zp,
+    const void* d_b_zp, int b_zp_per_col, const int32_t* d_rowsum_a,
+    int32_t* d_out) {
+  ICX_REQUIRE(is_8bit(a_type), "MatMulInteger: input a must be Int8 or UInt8");
+  ICX_REQUIRE(is_8bit(b_type), "MatMulInteger: input b must be Int8 or UInt8");
+  ICX_REQUIRE(M < (1u << 31) && N < (1u << 30) && K < (1u << 30),
+              "MatMulInteger: shape too large");
+  if (M == 0 || N == 0) return ICX_OK;
+  ICX_REQUIRE(d_out && d_colsum && (K == 0 || (d_a && d_bt)),
+              "MatMulInteger: null operand");
+  ICX_REQUIRE(d_b_zp == nullptr || d_rowsum_a != nullptr,
+              "MatMulInteger: b_zero_point needs the row sums of a");
+  GemmArgs g{};
+  g.M = (int)M; g.N = (int)N; g.K = (int)K;
+  g.a_zp = d_a_zp; g.a_zp_signed = a_type == ICX_S8;
+  g.b_zp = d_b_zp; g.b_zp_signed = b_type == ICX_S8; g.b_zp_per_col = b_zp_per_col;
+  g.colsum = d_colsum; g.rowsum = d_rowsum_a;
+  g.out = d_out;
+  cudaStream_t s = as_stream(stream);
+  if (K == 0) {
+    // empty reduction: every output is K*za*zb = 0
+    ICX_CUDA(cudaMemsetAsync(d_out, 0, M * N * 4, s));
+    return ICX_OK;
+  }
+  return launch_gemm<kEpiS32>(s, d_a, a_type == ICX_S8, d_bt, b_type == ICX_S8, g);
+}
+
+extern "C" int icx_matmul_integer(void* stream, const void* d_a, int a_type,
+                                  const void* d_b, int b_type, size_t M,
+                                  size_t K, size_t N, const void* d_a_zp,
+                                  const void* d_b_zp, int b_zp_per_col,
+                                  int32_t* d_out, void* d_workspace,
+                                  size_t workspace_bytes) {
+  ICX_REQUIRE(is_8bit(a_type), "MatMulInteger: input a must be Int8 or UInt8");
+  ICX_REQUIRE(is_8bit(b_type), "MatMulInteger: input b must be Int8 or UInt8");
+  const size_t need = icx_matmul_integer_workspace_bytes(M, K, N);
+  ICX_REQUIRE(d_workspace && workspace_bytes >= need,
+              "MatMulInteger: workspace %zu bytes < %zu required", workspace_bytes, need);
+  uint8_t* ws = static_cast<uint8_t*>(d_workspace);
+  void* bt = ws;
+  int32_t* colsum = reinterpret_cast<int32_t*>(ws + align256(N * K));
+  int32_t* rowsum = reinterpret_cast<int32_t*>(ws + align256(N * K) + align256(N * 4));
+  int rc = icx_prepare_b(stream, d_b, b_type, K, N, bt, colsum);
+  if (rc) return rc;
+  if (d_b_zp && M && K) {
+    const int threads = 256;
+    const size_t blocks = (M * 32 + threads - 1) / threads;
+    rowsum_kernel<<<(unsigned)blocks, threads, 0, as_stream(stream)>>>(
+        static_cast<const uint8_t*>(d_a), a_type == ICX_S8, (int)M, (int)K, rowsum);
+    ICX_LAUNCH_CHECK();
+  } else if (d_b_zp && M) {
+    ICX_CUDA(cudaMemsetAsync(rowsum, 0, M * 4, as_stream(stream)));
+  }
+  return icx_matmul_integer_prepared(stream, d_a, a_type, bt, b_type, colsum, M, K, N,
+                                     d_a_zp, d_b_zp, b_zp_per_col, rowsum, d_out);
+}
+
+extern "C" int icx_quant_linear(void* stream, const uint8_t* d_q,
+                                const float* d_a_scale, const uint8_t* d_a_zp,
+                                const int32_t* d_rowsum_q, const int8_t* d_wt,
+                                const int32_t* d_colsum, size_t M, size_t K,
+                                size_t N, const float* d_w_scale,
+                                int w_scale_per_col, const int8_t* d_b_zp,
+                                int b_zp_per_col, const float* d_bias, int gelu,
+                                float* d_out) {
+  ICX_REQUIRE(M < (1u << 31) && N < (1u << 30) && K < (1u << 30),
+              "QuantLinear: shape too large");
+  if (M == 0 || N == 0) return ICX_OK;
+  ICX_REQUIRE(d_out && d_colsum && d_a_scale && d_w_scale && (K == 0 || (d_q && d_wt)),
+              "QuantLinear: null operand");
+  ICX_REQUIRE(d_b_zp == nullptr || d_rowsum_q != nullptr,
+              "QuantLinear: b_zero_point needs the row sums of q");
+  ICX_REQUIRE(K > 0, "QuantLinear: K must be positive");
+  GemmArgs g{};
+  g.M = (int)M; g.N = (int)N; g.K = (int)K;
+  g.a_zp = d_a_zp; g.a_zp_signed = 0;
+  g.b_zp = d_b_zp; g.b_zp_signed = 1; g.b_zp_per_col = b_zp_per_col;
+  g.colsum = d_colsum; g.rowsum = d_rowsum_q;
+  g.a_scale = d_a_scale; g.w_scale = d_w_scale; g.w_scale_per_col = w_scale_per_col;
+  g.bias = d_bias;
+  g.out = d_out;
+  cudaStream_t s = as_stream(stream);
+  return gelu ? launch_gemm<kEpiGelu>(s, d_q, false, d_wt, true, g)
+              : launch_gemm<kEpiF32>(s, d_q, false, d_wt, true, g);
+}

@@ -1,0 +1,170 @@
+/*
+ * iconnx_b200 — C ABI of the B200 (sm_100a) int8 dynamic-quantization path.
+ *
+ * The path is the ONNX Runtime style chain every int8 Linear layer lowers to:
+ *   DynamicQuantizeLinear -> MatMulInteger -> Cast -> Mul(scale) -> Add(bias)
+ *   [-> erf-GELU]
+ * Each entry point below replaces one interface of the reference engine
+ * (iconnx, a Rust crate); the citation names the file:line it replaces.
+ *
+ * Conventions
+ *   - Every function returns an int status: ICX_OK (0) or a negative
+ *     ICX_ERR_* code.  icx_last_error() returns a thread-local message for the
+ *     most recent failure on the calling thread.  No entry point aborts,
+ *     panics or traps; invalid arguments are rejected before any launch
+ *     (mirrors CudaError::Kernel in src/cuda/context.rs:295-325).
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default
+ *     stream).  All work is enqueued asynchronously on it.
+ *   - Pointers named d_* are device pointers owned by the caller.  The
+ *     kernel entry points never allocate; scratch space is passed in as a
+ *     caller-owned workspace whose size a *_workspace_bytes query returns.
+ *   - Matrices are row-major and contiguous.
+ *   - Element type codes: ICX_U8, ICX_S8, ICX_S32, ICX_F32.
+ */
+#ifndef ICONNX_B200_H
+#define ICONNX_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define ICX_API __attribute__((visibility("default")))
+#else
+#define ICX_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+#define ICX_OK 0
+#define ICX_ERR_INVALID (-1)     /* bad argument: dtype, rank, shape, null */
+#define ICX_ERR_CUDA (-2)        /* a CUDA runtime/driver call failed       */
+#define ICX_ERR_UNSUPPORTED (-3) /* valid ONNX, not supported by this path  */
+#define ICX_ERR_WORKSPACE (-4)   /* workspace too small                     */
+#define ICX_ERR_SHAPE_MISMATCH (-5) /* input shape differs from the plan    */
+#define ICX_ERR_NOT_FOUND (-6)   /* unknown tensor / output name            */
+
+/* device-side status values (icx_device_status) */
+#define ICX_DEVICE_TIMEOUT_PRODUCER 0x101
+#define ICX_DEVICE_TIMEOUT_MMA 0x102
+#define ICX_DEVICE_TIMEOUT_EPILOGUE 0x103
+
+/* ---- element types ----------------------------------------------------- */
+#define ICX_U8 0
+#define ICX_S8 1
+#define ICX_S32 2
+#define ICX_F32 3
+
+/* Message for the last failing call on this thread ("" if none). */
+ICX_API const char* icx_last_error(void);
+
+/* Library version string. */
+ICX_API const char* icx_version(void);
+
+/* Reads and clears the device-side status word of `device` (0 = no kernel
+ * gave up on a bounded wait since the last call). */
+ICX_API int icx_device_status(int device, int* status_out);
+
+/* ======================================================================== *
+ * DynamicQuantizeLinear
+ * Replaces gpu_dynamic_quantize_linear (src/cuda/ops/quantize.rs:296-377),
+ * which the reference runs on the host, and follows the CPU forward
+ * (src/operators/dynamic_quantize_linear.rs:32-112) bit for bit:
+ *   min/max over x and 0 (NaN skipped), scale = (max-min)/255 in f64,
+ *   zp = clamp(rte(0 - min/scale)), y = clamp(rte(x/scale) + zp) in f64,
+ *   min == max -> scale 0, zp 0, y 0.
+ * Outputs: d_y u8[n], d_scale f32[1], d_zp u8[1].
+ * Optional side output: d_rowsum s32[n/row_len] = per-row sum of y, used by
+ * the per-column weight zero-point correction of the GEMM (pass NULL to
+ * skip; row_len must divide n when it is given).
+ * ======================================================================== */
+ICX_API size_t icx_dql_workspace_bytes(size_t n);
+
+ICX_API int icx_dql_f32_u8(void* stream, const float* d_x, size_t n, uint8_t* d_y,
+                   float* d_scale, uint8_t* d_zp, int32_t* d_rowsum,
+                   size_t row_len, void* d_workspace, size_t workspace_bytes);
+
+/* ======================================================================== *
+ * Weight preparation for MatMulInteger.
+ * Transposes b [K, N] (u8 or s8) into the tensor-core operand layout
+ * bt [N, K] and writes colsum[n] = sum_k b[k, n] (as the element type's
+ * integer value).  Done once per weight at plan build time; the per-op
+ * MatMulInteger entry point calls it on its workspace.
+ * ======================================================================== */
+ICX_API int icx_prepare_b(void* stream, const void* d_b, int b_type, size_t K,
+                  size_t N, void* d_bt, int32_t* d_colsum);
+
+/* ======================================================================== *
+ * MatMulInteger, int32 output.
+ * Replaces gpu_matmul_integer (src/cuda/ops/quantize.rs:398-615) and its
+ * kernels matmul_integer_{u8s8,s8s8,s8u8,u8u8}_kernel
+ * (src/cuda/ops/quantize_kernels.rs:116-194):
+ *   out[m, n] = sum_k (a[m,k] - a_zp) * (b[k,n] - b_zp[n])   (wrapping s32)
+ * a: [M, K] (u8 or s8); b: [K, N] (u8 or s8) row-major as in ONNX.
+ * d_a_zp: NULL or one element of a's type; d_b_zp: NULL, one element, or
+ * N elements (b_zp_per_col != 0; the ONNX per-column form the reference
+ * rejects in src/cuda/ops/quantize.rs:625-658).  Zero points stay on the
+ * device (no host round trip, unlike resolve_scalar_zp :625-679).
+ * Uses workspace for the transposed b, its column sums and row sums of a.
+ * ======================================================================== */
+ICX_API size_t icx_matmul_integer_workspace_bytes(size_t M, size_t K, size_t N);
+
+ICX_API int icx_matmul_integer(void* stream, const void* d_a, int a_type,
+                       const void* d_b, int b_type, size_t M, size_t K,
+                       size_t N, const void* d_a_zp, const void* d_b_zp,
+                       int b_zp_per_col, int32_t* d_out, void* d_workspace,
+                       size_t workspace_bytes);
+
+/* Same GEMM on an already prepared weight (bt [N, K] + colsum from
+ * icx_prepare_b).  d_rowsum_a (s32[M]) is required when d_b_zp != NULL. */
+ICX_API int icx_matmul_integer_prepared(void* stream, const void* d_a, int a_type,
+                                const void* d_bt, int b_type,
+                                const int32_t* d_colsum, size_t M, size_t K,
+                                size_t N, const void* d_a_zp,
+                                const void* d_b_zp, int b_zp_per_col,
+                                const int32_t* d_rowsum_a, int32_t* d_out);
+
+/* ======================================================================== *
+ * Fused quantized Linear: MatMulInteger -> Cast -> Mul -> Add [-> GELU].
+ * Replaces the per-op chain the reference executes for one int8 Linear
+ * (src/cuda/executor/layout.rs:1034-1097 MatMulInteger, layout.rs:144 Cast,
+ * src/cuda/executor/elementwise.rs:123 Mul and :54 Add with their
+ * gpu_expand broadcasts, src/cuda/kernels/mod.rs:246 erf_kernel for GELU):
+ *   acc   = sum_k (q[m,k] - a_zp) * (w[k,n] - b_zp[n])          (s32)
+ *   s[n]  = f32(a_scale) * w_scale[n]                             (one f32 mul)
+ *   out   = f32(acc) * s[n] + bias[n]                             (no FMA)
+ *   gelu: out = (out * (1 + erf(out / sqrt2))) * 0.5
+ * q: u8 [M, K] from DynamicQuantizeLinear; a_scale/a_zp: its device
+ * outputs; wt/colsum: prepared weight; w_scale: 1 or N floats; b_zp: NULL,
+ * 1 or N s8 values; bias: N floats (or NULL); out: f32 [M, N].
+ * The s32 accumulator never leaves the SM: it lives in tensor memory.
+ * ======================================================================== */
+ICX_API int icx_quant_linear(void* stream, const uint8_t* d_q, const float* d_a_scale,
+                     const uint8_t* d_a_zp, const int32_t* d_rowsum_q,
+                     const int8_t* d_wt, const int32_t* d_colsum, size_t M,
+                     size_t K, size_t N, const float* d_w_scale,
+                     int w_scale_per_col, const int8_t* d_b_zp,
+                     int b_zp_per_col, const float* d_bias, int gelu,
+                     float* d_out);
+
+/* ======================================================================== *
+ * DequantizeLinear: y = (f32(x) - f32(zp)) * scale, per tensor or per axis.
+ * Replaces gpu_dequantize_linear (src/cuda/ops/quantize.rs:24-267) and
+ * dequantize_linear_{i8,u8,i32}_kernel (src/cuda/ops/quantize_kernels.rs:
+ * 52-81); arithmetic follows the CPU forward
+ * (src/operators/dequantize_linear.rs:32-179).
+ * The tensor is viewed as [outer, axis_len, inner]; scale/zp have
+ * scale_len elements (1 = per tensor, axis_len = per axis).
+ * ======================================================================== */
+ICX_API int icx_dequantize_linear(void* stream, const void* d_x, int x_type,
+                          size_t outer, size_t axis_len, size_t inner,
+                          const float* d_scale, size_t scale_len,
+                          const void* d_zp, float* d_y);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ICONNX_B200_H */
