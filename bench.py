@@ -129,14 +129,17 @@ class FfnWorkload:
         self.out_host = torch.empty((self.M, hidden), dtype=torch.float32).pin_memory()
         self.units_per_step = batch  # sequences
         self.unit = "seq/s"
-        self.launches_per_step = 6   # 2 x (minmax, quantize, fused GEMM)
+        self.launches_per_step = 5   # minmax, quantize, GEMM1(+minmax of h), quantize, GEMM2
         self.gemm_ops = 2 * (2.0 * self.M * hidden * ffn)
 
     def step(self, x=None):
         ops = self.ops
+        if not hasattr(self, "mm"):
+            self.mm = ops.MinMaxPartials(self.device)
+        # GEMM1's epilogue records the (min, max) partials DQL2 needs
         h, *_ = ops.dynamic_quant_linear(self.x if x is None else x, self.w1, self.ws, self.b1,
-                                         gelu=True)
-        out, *_ = ops.dynamic_quant_linear(h, self.w2, self.ws, self.b2)
+                                         gelu=True, out_minmax=self.mm)
+        out, *_ = ops.dynamic_quant_linear(h, self.w2, self.ws, self.b2, x_minmax=self.mm)
         return out
 
     def e2e_step(self):
@@ -351,6 +354,13 @@ def main():
     barrier()
     clocks = ClockSampler(local)
     clocks.start()
+    # keep the GPU under the same load for ~1.5 s so the 100 ms clock sampler
+    # sees the clocks of this workload (untimed, like the warm-up)
+    t_soak = time.time()
+    while time.time() - t_soak < 1.5:
+        for _ in range(20):
+            g.replay()
+        torch.cuda.synchronize(dev)
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
            for _ in range(args.steps)]
     for s, e in evs:

@@ -14,6 +14,7 @@ SO_PATH = os.path.join(HERE, "libiconnx_b200.so")
 HEADER = os.path.join(os.path.dirname(HERE), "include", "iconnx_b200.h")
 
 ICX_OK = 0
+ICX_MAX_MINMAX_PARTIALS = 1184
 ICX_U8, ICX_S8, ICX_S32, ICX_F32 = 0, 1, 2, 3
 
 _vp, _sz, _i = ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int
@@ -31,7 +32,8 @@ PROTOTYPES = {
     "icx_matmul_integer_prepared": (_i, [_vp, _vp, _i, _vp, _i, _vp, _sz, _sz, _sz, _vp, _vp, _i,
                                          _vp, _vp]),
     "icx_quant_linear": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _sz, _sz, _vp, _i, _vp, _i,
-                              _vp, _i, _vp]),
+                              _vp, _i, _vp, _vp, _vp]),
+    "icx_dql_quantize_f32_u8": (_i, [_vp, _vp, _sz, _vp, _i, _vp, _vp, _vp, _vp, _sz]),
     "icx_dequantize_linear": (_i, [_vp, _vp, _i, _sz, _sz, _sz, _vp, _sz, _vp, _vp]),
 }
 

@@ -9,8 +9,9 @@
 //      optional row-sum output.
 //   2. dql_quantize_kernel: every block folds the partials (a few KB, L2
 //      resident), derives scale/zero-point in f64 exactly as the reference
-//      does, then quantises 16 elements per thread (four 16-byte loads, one
-//      16-byte store) and optionally accumulates per-row sums of y.
+//      does, then quantises 512 elements per warp iteration (four coalesced
+//      512-byte loads, four coalesced 128-byte stores) and optionally
+//      accumulates per-row sums of y.
 //
 // Exactness of the per-element quantisation.  The reference computes
 // rte(f64(x) / scale) with an f64 division.  Here t = x * f32(1/scale) is
@@ -27,7 +28,7 @@ namespace icx {
 
 constexpr int kMinmaxThreads = 512;
 constexpr int kQuantThreads = 256;
-constexpr int kMaxPartials = 148 * 8;
+constexpr int kMaxPartials = ICX_MAX_MINMAX_PARTIALS;
 
 __device__ __forceinline__ void warp_minmax(float& mn, float& mx) {
 #pragma unroll
@@ -186,35 +187,33 @@ __global__ void __launch_bounds__(kQuantThreads)
 
   size_t done = 0;
   if (vec16) {
-    // 16 elements per thread; a chunk never straddles a row because the
-    // host only selects this path when row_len % 16 == 0 (or no row sums).
-    const size_t nchunks = n / 16;
+    // Each warp quantises 512 consecutive elements per iteration: four fully
+    // coalesced 512-byte float4 loads (lane l takes float4 32*j + l) and four
+    // coalesced 128-byte stores of the packed u8 words.  A 4-element word
+    // never straddles a row because the host selects this path only when
+    // row_len % 4 == 0 (or no row sums are requested).
+    const size_t nblk = n / 512;
     const float4* x4 = reinterpret_cast<const float4*>(x);
-    uint4* y16 = reinterpret_cast<uint4*>(y);
-    for (size_t base = warp_g * 32; base < nchunks; base += nwarps * 32) {
-      const size_t c = base + lane;
-      const bool valid = c < nchunks;
-      uint32_t sum = 0;
-      if (valid) {
-        float4 v0 = __ldg(x4 + 4 * c), v1 = __ldg(x4 + 4 * c + 1),
-               v2 = __ldg(x4 + 4 * c + 2), v3 = __ldg(x4 + 4 * c + 3);
-        uint4 o;
-        o.x = quant4(v0, p, sum);
-        o.y = quant4(v1, p, sum);
-        o.z = quant4(v2, p, sum);
-        o.w = quant4(v3, p, sum);
-        y16[c] = o;
-      }
-      if (rowsum != nullptr) {
-        const unsigned long long row =
-            valid ? (unsigned long long)(c * 16 / row_len) : ~0ull;
-        const unsigned mask = __match_any_sync(0xffffffffu, row);
-        const uint32_t tot = __reduce_add_sync(mask, sum);
-        if (valid && lane == __ffs(mask) - 1)
-          atomicAdd(rowsum + row, (int32_t)tot);
+    uint32_t* y4 = reinterpret_cast<uint32_t*>(y);
+    for (size_t blk = warp_g; blk < nblk; blk += nwarps) {
+      const size_t base4 = blk * 128;
+      float4 v[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) v[j] = __ldg(x4 + base4 + 32 * j + lane);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        uint32_t sum = 0;
+        y4[base4 + 32 * j + lane] = quant4(v[j], p, sum);
+        if (rowsum != nullptr) {
+          const unsigned long long row =
+              (unsigned long long)((base4 + 32 * j + lane) * 4 / row_len);
+          const unsigned mask = __match_any_sync(0xffffffffu, row);
+          const uint32_t tot = __reduce_add_sync(mask, sum);
+          if (lane == __ffs(mask) - 1) atomicAdd(rowsum + row, (int32_t)tot);
+        }
       }
     }
-    done = nchunks * 16;
+    done = nblk * 512;
   }
   // scalar path: misaligned buffers, rows not a multiple of 16, and tails
   const size_t tid = (size_t)blockIdx.x * kQuantThreads + threadIdx.x;
@@ -232,6 +231,14 @@ static int minmax_blocks(size_t n) {
   if (b < 1) b = 1;
   if (b > (size_t)kMaxPartials) b = kMaxPartials;
   return (int)b;
+}
+
+int dql_minmax_partials(size_t n) { return minmax_blocks(n); }
+
+int launch_dql_minmax(cudaStream_t s, const float* x, size_t n, float2* partials) {
+  dql_minmax_kernel<<<minmax_blocks(n), kMinmaxThreads, 0, s>>>(x, n, partials, nullptr, 0);
+  ICX_LAUNCH_CHECK();
+  return ICX_OK;
 }
 
 }  // namespace icx
@@ -263,7 +270,7 @@ extern "C" int icx_dql_f32_u8(void* stream, const float* d_x, size_t n,
   ICX_LAUNCH_CHECK();
   const bool aligned = ((reinterpret_cast<uintptr_t>(d_x) |
                          reinterpret_cast<uintptr_t>(d_y)) & 15) == 0;
-  const int vec16 = aligned && (d_rowsum == nullptr || row_len % 16 == 0);
+  const int vec16 = aligned && (d_rowsum == nullptr || row_len % 4 == 0);
   size_t work = vec16 ? n / 16 : n;
   size_t qb = (work + kQuantThreads - 1) / kQuantThreads;
   if (qb < 1) qb = 1;
@@ -271,6 +278,33 @@ extern "C" int icx_dql_f32_u8(void* stream, const float* d_x, size_t n,
   dql_quantize_kernel<<<(int)qb, kQuantThreads, 0, s>>>(
       d_x, n, static_cast<const float2*>(d_workspace), blocks, d_y, d_scale,
       d_zp, d_rowsum, row_len ? row_len : 1, vec16);
+  ICX_LAUNCH_CHECK();
+  return ICX_OK;
+}
+
+extern "C" int icx_dql_quantize_f32_u8(void* stream, const float* d_x, size_t n,
+                                       const float* d_minmax, int n_minmax,
+                                       uint8_t* d_y, float* d_scale, uint8_t* d_zp,
+                                       int32_t* d_rowsum, size_t row_len) {
+  ICX_REQUIRE(d_scale && d_zp, "DynamicQuantizeLinear: null scale/zp output");
+  ICX_REQUIRE(n == 0 || (d_x && d_y), "DynamicQuantizeLinear: null x or y");
+  ICX_REQUIRE(d_minmax != nullptr && n_minmax >= 1 && n_minmax <= ICX_MAX_MINMAX_PARTIALS,
+              "DynamicQuantizeLinear: need 1..%d (min, max) partials, got %d",
+              ICX_MAX_MINMAX_PARTIALS, n_minmax);
+  ICX_REQUIRE(d_rowsum == nullptr || (row_len > 0 && n % row_len == 0),
+              "DynamicQuantizeLinear: row_len %zu must divide n %zu", row_len, n);
+  cudaStream_t s = as_stream(stream);
+  if (d_rowsum) ICX_CUDA(cudaMemsetAsync(d_rowsum, 0, (n / row_len) * sizeof(int32_t), s));
+  const bool aligned = ((reinterpret_cast<uintptr_t>(d_x) |
+                         reinterpret_cast<uintptr_t>(d_y)) & 15) == 0;
+  const int vec16 = aligned && (d_rowsum == nullptr || row_len % 4 == 0);
+  size_t work = vec16 ? n / 16 : n;
+  size_t qb = (work + kQuantThreads - 1) / kQuantThreads;
+  if (qb < 1) qb = 1;
+  if (qb > 148 * 8) qb = 148 * 8;
+  dql_quantize_kernel<<<(int)qb, kQuantThreads, 0, s>>>(
+      d_x, n, reinterpret_cast<const float2*>(d_minmax), n_minmax, d_y, d_scale, d_zp,
+      d_rowsum, row_len ? row_len : 1, vec16);
   ICX_LAUNCH_CHECK();
   return ICX_OK;
 }

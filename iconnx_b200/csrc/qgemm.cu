@@ -24,6 +24,7 @@
 // The tensor cores compute sum_k a*b on the raw u8/s8 values.
 #include <cuda.h>
 
+#include <cstring>
 #include <mutex>
 #include <unordered_map>
 
@@ -32,11 +33,13 @@
 
 namespace icx {
 
+// from dql.cu
+int dql_minmax_partials(size_t n);
+int launch_dql_minmax(cudaStream_t s, const float* x, size_t n, float2* partials);
+
 constexpr int kBM = 128;      // rows per tile (UMMA M)
 constexpr int kBK = 128;      // K bytes per stage (one 128-byte swizzle atom)
 constexpr int kUmmaK = 32;    // K per tcgen05.mma kind::i8
-constexpr int kThreads = 192; // 6 warps
-constexpr int kEpiThreads = 128;
 
 enum EpiMode { kEpiS32 = 0, kEpiF32 = 1, kEpiGelu = 2 };
 
@@ -54,17 +57,8 @@ struct GemmArgs {
   int w_scale_per_col;
   const float* bias;      // nullable, N
   void* out;              // s32 or f32 [M, N]
-};
-
-template <int BN>
-struct Cfg {
-  static constexpr int kStages = BN == 256 ? 4 : 6;
-  static constexpr int kABytes = kBM * kBK;
-  static constexpr int kBBytes = BN * kBK;
-  static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kTmemCols = 2 * BN;
-  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ +
-                                    256 /*barriers*/ + 4 * BN * 4 /*params*/;
+  float2* minmax;         // nullable: per-CTA (min, max) of the f32 output,
+                          // seeded with 0 like DynamicQuantizeLinear's scan
 };
 
 __device__ __forceinline__ int32_t ld_zp(const void* p, int is_signed,
@@ -74,51 +68,112 @@ __device__ __forceinline__ int32_t ld_zp(const void* p, int is_signed,
 }
 
 // Erf-GELU 0.5*x*(1+erf(x/sqrt2)) with the Abramowitz & Stegun 7.1.26 erf
-// the reference uses (src/operators/erf.rs:30-40), evaluated with fused
-// multiply-adds and the hardware exp2: within ~1e-6 absolute of the
-// reference's op-by-op f32 evaluation (tested bound 1e-5).
+// the reference uses (src/operators/erf.rs:30-40):
+//   erf(d) = sign(d) * (1 - Q),  Q = t*P(t)*exp(-d^2),  t = 1/(1 + p|d|)
+// so  GELU(x) = x - x*Q/2  (x >= 0)  or  x*Q/2  (x < 0).
+// With u = x * sqrt(log2 e)/sqrt2, exp(-d^2) = 2^(-u^2) and p|d| = k2|u|;
+// the 1/2 is folded into the polynomial coefficients (exact power-of-two
+// scaling of the reference's f32 literals).  Hardware rcp/ex2 and fused
+// multiply-adds keep this within ~1e-6 absolute of the reference's op-by-op
+// f32 evaluation (the tests bound it by 1e-5).
 __device__ __forceinline__ float gelu_erf(float x) {
-  const float d = x * 0.70710678118654752f;
-  const float a = fabsf(d);
-  const float t = __frcp_rn(fmaf(0.3275911f, a, 1.0f));
-  float p = fmaf(1.0614054f, t, -1.4531521f);
-  p = fmaf(p, t, 1.4214138f);
-  p = fmaf(p, t, -0.28449672f);
-  p = fmaf(p, t, 0.2548296f);
-  p = p * t;
-  const float e = __expf(-a * a);
-  const float erf_abs = fmaf(-p, e, 1.0f);
-  const float erf_v = copysignf(erf_abs, d);
-  return (x * (1.0f + erf_v)) * 0.5f;
+  const float u = x * 0.8493217825889587f;          // x/sqrt2 * sqrt(log2 e)
+  float t;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t) : "f"(fmaf(0.2727374732494354f, fabsf(u), 1.0f)));
+  float e;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(-(u * u)));
+  float p = fmaf(0.5307027f, t, -0.72657605f);      // 0.5 * A&S coefficients
+  p = fmaf(p, t, 0.7107069f);
+  p = fmaf(p, t, -0.14224836f);
+  p = fmaf(p, t, 0.1274148f);
+  const float hq = (p * t) * e;                      // Q/2
+  const float xq = x * hq;
+  return u >= 0.0f ? x - xq : xq;
 }
 
-// Named barrier among the 4 epilogue warps only.
+constexpr int kEpiWarps = 8;                       // 2 per TMEM lane quadrant
+constexpr int kThreads = 64 + 32 * kEpiWarps;        // producer + MMA + epilogue
+constexpr int kStageOutBytes = 32 * 32 * 4;          // one warp's 32x32 output box
+
+template <int BN>
+struct Cfg {
+  static constexpr int kStages = BN == 256 ? 4 : 6;
+  static constexpr int kABytes = kBM * kBK;
+  static constexpr int kBBytes = BN * kBK;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kTmemCols = 2 * BN;
+  static constexpr int kOutOffset = kStages * kStageBytes;
+  static constexpr int kBarOffset = kOutOffset + kEpiWarps * kStageOutBytes;
+  // barriers (2*stages + 4) * 8 B, the TMEM slot, 8 (min,max) pairs
+  static constexpr int kSmemBytes = kBarOffset + 256 + 1024 /*align slack*/;
+  static_assert((2 * kStages + 4) * 8 + 8 + kEpiWarps * 8 <= 256, "barrier area");
+};
+
+// Named barrier among the epilogue warps only.
 __device__ __forceinline__ void epi_sync() {
-  asm volatile("bar.sync 1, 128;" ::: "memory");
+  asm volatile("bar.sync 1, %0;" ::"n"(32 * kEpiWarps) : "memory");
 }
 
-template <int BN, int EPI>
+// 2-D TMA store shared -> global of one 32x32 box (tracked by bulk groups).
+__device__ __forceinline__ void tma_store_2d(const void* tmap, const void* src,
+                                             int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+          tmap),
+      "r"(smem_addr(src)), "r"(c0), "r"(c1)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_read0() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait0() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
+template <int EPI, bool HAS_BIAS>
+__device__ __forceinline__ uint32_t finish1(int32_t v, float sc, float bi) {
+  if (EPI == kEpiS32) return (uint32_t)v;
+  float f = __fmul_rn(__int2float_rn(v), sc);
+  if (HAS_BIAS) f = __fadd_rn(f, bi);
+  if (EPI == kEpiGelu) f = gelu_erf(f);
+  return __float_as_uint(f);
+}
+
+// Loads 4 consecutive elements starting at column n (n % 4 == 0) with
+// zero fill past N; `vec` says 16-byte vector loads are legal.
+__device__ __forceinline__ int4 ld4i(const int32_t* p, int n, int N, bool vec) {
+  if (vec && n + 4 <= N) return __ldg(reinterpret_cast<const int4*>(p + n));
+  return make_int4(n < N ? p[n] : 0, n + 1 < N ? p[n + 1] : 0, n + 2 < N ? p[n + 2] : 0,
+                   n + 3 < N ? p[n + 3] : 0);
+}
+__device__ __forceinline__ float4 ld4f(const float* p, int n, int N, bool vec) {
+  if (vec && n + 4 <= N) return __ldg(reinterpret_cast<const float4*>(p + n));
+  return make_float4(n < N ? p[n] : 0.f, n + 1 < N ? p[n + 1] : 0.f, n + 2 < N ? p[n + 2] : 0.f,
+                     n + 3 < N ? p[n + 3] : 0.f);
+}
+
+template <int BN, int EPI, bool HAS_BZ, bool HAS_BIAS>
 __global__ void __launch_bounds__(kThreads, 1)
     qgemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA,
                          const __grid_constant__ CUtensorMap tmB,
-                         const GemmArgs args, uint32_t idesc) {
+                         const __grid_constant__ CUtensorMap tmOut,
+                         const GemmArgs args, uint32_t idesc, int tma_store, int vec_cols) {
   using C = Cfg<BN>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + C::kStages * C::kABytes;
-  uint64_t* bars =
-      reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStageBytes);
+  uint8_t* sOut = smem + C::kOutOffset;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kBarOffset);
   uint64_t* full = bars;
   uint64_t* empty = bars + C::kStages;
   uint64_t* tfull = bars + 2 * C::kStages;
   uint64_t* tempty = tfull + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
-  int32_t* s_corr = reinterpret_cast<int32_t*>(smem + C::kStages * C::kStageBytes + 256);
-  int32_t* s_bz = s_corr + BN;
-  float* s_scale = reinterpret_cast<float*>(s_bz + BN);
-  float* s_bias = s_scale + BN;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -135,7 +190,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 4);
+      mbar_init(&tempty[a], kEpiWarps);
     }
     fence_barrier_init();
     fence_proxy_async_smem();
@@ -143,6 +198,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    if (tma_store) tma_prefetch_desc(&tmOut);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, C::kTmemCols);
@@ -217,91 +273,162 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ----------------------------------------------------------- epilogue
-    const int quad = warp & 3;             // TMEM lanes [32*quad, 32*quad+32)
-    const int et = threadIdx.x - 64;       // 0..127
-    const int row_in_tile = quad * 32 + lane;
-    int32_t za = 0;
-    float a_scale = 0.0f;
-    if (args.a_zp) za = ld_zp(args.a_zp, args.a_zp_signed, 0);
-    if (EPI != kEpiS32) a_scale = *args.a_scale;
-    const bool has_bz = args.b_zp != nullptr;
+    const int e = warp - 2;                       // 0..kEpiWarps-1
+    const int quad = warp & 3;                    // TMEM lanes [32*quad, 32*quad+32)
+    const int part = e >> 2;                      // which chunks of the quadrant
+    constexpr int kParts = kEpiWarps / 4;
+    uint8_t* stage_out = sOut + e * kStageOutBytes;
+    const uint32_t za = args.a_zp ? (uint32_t)ld_zp(args.a_zp, args.a_zp_signed, 0) : 0u;
+    float a_scale = 0.0f, sc_scalar = 0.0f;
+    if (EPI != kEpiS32) {
+      a_scale = *args.a_scale;
+      sc_scalar = __fmul_rn(a_scale, args.w_scale[0]);
+    }
+    const bool sc_per_col = args.w_scale_per_col != 0;
+    const bool bz_per_col = args.b_zp_per_col != 0;
+    const int32_t bz_scalar = HAS_BZ ? ld_zp(args.b_zp, args.b_zp_signed, 0) : 0;
+    const bool vec = vec_cols != 0;
     int acc = 0;
     uint32_t acc_phase = 0;
-    bool ok = true;  // false once a bounded wait gave up: skip work, keep barriers matched
+    bool ok = true;  // false once a bounded wait gave up: skip work
+    const bool track = (EPI != kEpiS32) && args.minmax != nullptr;
+    float run_mn = 0.0f, run_mx = 0.0f;  // the DynamicQuantizeLinear seed
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
       const int m0 = (t / num_n) * kBM;
       const int n0 = (t % num_n) * BN;
-      // per-column constants of this tile
-      for (int j = et; j < BN; j += kEpiThreads) {
-        const int n = n0 + j;
-        int32_t cs = 0, bz = 0;
-        float sc = 0.0f, bi = 0.0f;
-        if (n < N) {
-          cs = args.colsum[n];
-          if (has_bz) bz = ld_zp(args.b_zp, args.b_zp_signed, args.b_zp_per_col ? n : 0);
-          if (EPI != kEpiS32) {
-            sc = __fmul_rn(a_scale, args.w_scale[args.w_scale_per_col ? n : 0]);
-            bi = args.bias ? args.bias[n] : 0.0f;
+      const int mrow0 = m0 + quad * 32;
+      const int m = mrow0 + lane;
+      uint32_t kza_rs = 0;
+      if (HAS_BZ) kza_rs = (uint32_t)K * za - ((m < M) ? (uint32_t)args.rowsum[m] : 0u);
+      // pull this tile's per-column operands into L1 while the MMA runs
+      {
+        const int et = threadIdx.x - 64;
+        const int lines = BN * 4 / 128;  // 128-byte lines per operand array
+        if (et < lines) {
+          const int n = n0 + et * 32;
+          if (n < N) {
+            asm volatile("prefetch.global.L1 [%0];" ::"l"(args.colsum + n));
+            if (EPI != kEpiS32 && HAS_BIAS) asm volatile("prefetch.global.L1 [%0];" ::"l"(args.bias + n));
+            if (EPI != kEpiS32 && sc_per_col) asm volatile("prefetch.global.L1 [%0];" ::"l"(args.w_scale + n));
           }
         }
-        s_corr[j] = (int32_t)((uint32_t)K * (uint32_t)za * (uint32_t)bz -
-                              (uint32_t)za * (uint32_t)cs);
-        s_bz[j] = bz;
-        s_scale[j] = sc;
-        s_bias[j] = bi;
       }
-      epi_sync();
-      const int m = m0 + row_in_tile;
-      const int32_t rs = (has_bz && m < M) ? args.rowsum[m] : 0;
       if (ok) ok = mbar_wait(&tfull[acc], acc_phase, ICX_DEVICE_TIMEOUT_EPILOGUE);
       tc_fence_after();
       const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
 #pragma unroll 1
-      for (int c = 0; c < BN / 32 && ok; ++c) {
+      for (int c = part; c < BN / 32 && ok; c += kParts) {
+        const int nb = n0 + c * 32;
+        if (nb >= N) break;  // warp-uniform
+        const bool fast = vec && (nb + 32 <= N) && !(HAS_BZ && bz_per_col);
         uint32_t r[32];
         tmem_ld_32x32b_x32(t_row + (uint32_t)(c * 32), r);
         tmem_ld_wait();
-        const int nb = n0 + c * 32;
-        if (m < M && nb < N) {
-          const bool full_chunk = (nb + 32 <= N) && ((N & 3) == 0);
-          if (EPI == kEpiS32) {
-            int32_t* orow = static_cast<int32_t*>(args.out) + (size_t)m * N + nb;
-            int32_t v[32];
+        if (fast) {
+          // whole chunk in range, 16-byte aligned operand vectors
+          const int4* cs4 = reinterpret_cast<const int4*>(args.colsum + nb);
+          const float4* bi4 = reinterpret_cast<const float4*>(args.bias + nb);
+          const float4* ws4 = reinterpret_cast<const float4*>(args.w_scale + nb);
 #pragma unroll
-            for (int j = 0; j < 32; ++j)
-              v[j] = (int32_t)(r[j] + (uint32_t)s_corr[c * 32 + j] -
-                               (uint32_t)s_bz[c * 32 + j] * (uint32_t)rs);
-            if (full_chunk) {
-#pragma unroll
-              for (int j = 0; j < 32; j += 4)
-                *reinterpret_cast<int4*>(orow + j) = make_int4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-            } else {
-#pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (nb + j < N) orow[j] = v[j];
+          for (int q = 0; q < 8; ++q) {
+            const int4 cs = __ldg(cs4 + q);
+            float4 sc = make_float4(sc_scalar, sc_scalar, sc_scalar, sc_scalar);
+            if (EPI != kEpiS32 && sc_per_col) {
+              const float4 w = __ldg(ws4 + q);
+              sc = make_float4(__fmul_rn(a_scale, w.x), __fmul_rn(a_scale, w.y),
+                               __fmul_rn(a_scale, w.z), __fmul_rn(a_scale, w.w));
             }
-          } else {
-            float* orow = static_cast<float*>(args.out) + (size_t)m * N + nb;
-            float v[32];
+            float4 bi = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (EPI != kEpiS32 && HAS_BIAS) bi = __ldg(bi4 + q);
+            int32_t v0 = (int32_t)(r[4 * q + 0] - za * (uint32_t)cs.x);
+            int32_t v1 = (int32_t)(r[4 * q + 1] - za * (uint32_t)cs.y);
+            int32_t v2 = (int32_t)(r[4 * q + 2] - za * (uint32_t)cs.z);
+            int32_t v3 = (int32_t)(r[4 * q + 3] - za * (uint32_t)cs.w);
+            if (HAS_BZ) {
+              const uint32_t kb = kza_rs * (uint32_t)bz_scalar;
+              v0 = (int32_t)((uint32_t)v0 + kb);
+              v1 = (int32_t)((uint32_t)v1 + kb);
+              v2 = (int32_t)((uint32_t)v2 + kb);
+              v3 = (int32_t)((uint32_t)v3 + kb);
+            }
+            r[4 * q + 0] = finish1<EPI, HAS_BIAS>(v0, sc.x, bi.x);
+            r[4 * q + 1] = finish1<EPI, HAS_BIAS>(v1, sc.y, bi.y);
+            r[4 * q + 2] = finish1<EPI, HAS_BIAS>(v2, sc.z, bi.z);
+            r[4 * q + 3] = finish1<EPI, HAS_BIAS>(v3, sc.w, bi.w);
+          }
+        } else {
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const int n = nb + 4 * q;
+            const int4 cs = ld4i(args.colsum, n, N, false);
+            int4 bz = make_int4(bz_scalar, bz_scalar, bz_scalar, bz_scalar);
+            if (HAS_BZ && bz_per_col) {
+              bz.x = n < N ? ld_zp(args.b_zp, args.b_zp_signed, n) : 0;
+              bz.y = n + 1 < N ? ld_zp(args.b_zp, args.b_zp_signed, n + 1) : 0;
+              bz.z = n + 2 < N ? ld_zp(args.b_zp, args.b_zp_signed, n + 2) : 0;
+              bz.w = n + 3 < N ? ld_zp(args.b_zp, args.b_zp_signed, n + 3) : 0;
+            }
+            float4 sc = make_float4(sc_scalar, sc_scalar, sc_scalar, sc_scalar);
+            if (EPI != kEpiS32 && sc_per_col) {
+              const float4 w = ld4f(args.w_scale, n, N, false);
+              sc = make_float4(__fmul_rn(a_scale, w.x), __fmul_rn(a_scale, w.y),
+                               __fmul_rn(a_scale, w.z), __fmul_rn(a_scale, w.w));
+            }
+            float4 bi = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (EPI != kEpiS32 && HAS_BIAS) bi = ld4f(args.bias, n, N, false);
+            int32_t v0 = (int32_t)(r[4 * q + 0] - za * (uint32_t)cs.x);
+            int32_t v1 = (int32_t)(r[4 * q + 1] - za * (uint32_t)cs.y);
+            int32_t v2 = (int32_t)(r[4 * q + 2] - za * (uint32_t)cs.z);
+            int32_t v3 = (int32_t)(r[4 * q + 3] - za * (uint32_t)cs.w);
+            if (HAS_BZ) {
+              v0 = (int32_t)((uint32_t)v0 + kza_rs * (uint32_t)bz.x);
+              v1 = (int32_t)((uint32_t)v1 + kza_rs * (uint32_t)bz.y);
+              v2 = (int32_t)((uint32_t)v2 + kza_rs * (uint32_t)bz.z);
+              v3 = (int32_t)((uint32_t)v3 + kza_rs * (uint32_t)bz.w);
+            }
+            r[4 * q + 0] = finish1<EPI, HAS_BIAS>(v0, sc.x, bi.x);
+            r[4 * q + 1] = finish1<EPI, HAS_BIAS>(v1, sc.y, bi.y);
+            r[4 * q + 2] = finish1<EPI, HAS_BIAS>(v2, sc.z, bi.z);
+            r[4 * q + 3] = finish1<EPI, HAS_BIAS>(v3, sc.w, bi.w);
+          }
+        }
+        if (track && m < M) {
+          if (nb + 32 <= N) {
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
-              const int32_t iv = (int32_t)(r[j] + (uint32_t)s_corr[c * 32 + j] -
-                                           (uint32_t)s_bz[c * 32 + j] * (uint32_t)rs);
-              float f = __fmul_rn(__int2float_rn(iv), s_scale[c * 32 + j]);
-              if (args.bias) f = __fadd_rn(f, s_bias[c * 32 + j]);
-              if (EPI == kEpiGelu) f = gelu_erf(f);
-              v[j] = f;
+              run_mn = fminf(run_mn, __uint_as_float(r[j]));
+              run_mx = fmaxf(run_mx, __uint_as_float(r[j]));
             }
-            if (full_chunk) {
+          } else {
+            for (int j = 0; j < 32; ++j)
+              if (nb + j < N) {
+                run_mn = fminf(run_mn, __uint_as_float(r[j]));
+                run_mx = fmaxf(run_mx, __uint_as_float(r[j]));
+              }
+          }
+        }
+        if (tma_store) {
+          if (mrow0 < M) {
+            // the previous box of this warp must have been read out of smem
+            if (lane == 0) bulk_wait_read0();
+            __syncwarp();
+            uint8_t* row = stage_out + lane * 128;
 #pragma unroll
-              for (int j = 0; j < 32; j += 4)
-                *reinterpret_cast<float4*>(orow + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-            } else {
-#pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (nb + j < N) orow[j] = v[j];
+            for (int q = 0; q < 8; ++q)
+              *reinterpret_cast<uint4*>(row + ((q ^ (lane & 7)) << 4)) =
+                  make_uint4(r[4 * q], r[4 * q + 1], r[4 * q + 2], r[4 * q + 3]);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_2d(&tmOut, stage_out, nb, mrow0);
+              bulk_commit();
             }
           }
+        } else if (m < M) {
+          uint32_t* orow = static_cast<uint32_t*>(args.out) + (size_t)m * N + nb;
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (nb + j < N) orow[j] = r[j];
         }
       }
       tc_fence_before();
@@ -309,7 +436,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive(&tempty[acc]);
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
-      epi_sync();  // s_* params are rewritten for the next tile
+    }
+    if (tma_store && lane == 0) bulk_wait0();
+    if (track) {
+      // CTA-wide (min, max) of everything this CTA wrote: one partial per CTA
+      float2* red = reinterpret_cast<float2*>(tmem_slot + 2);  // 8-byte aligned slot area
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        run_mn = fminf(run_mn, __shfl_xor_sync(0xffffffffu, run_mn, o));
+        run_mx = fmaxf(run_mx, __shfl_xor_sync(0xffffffffu, run_mx, o));
+      }
+      if (lane == 0) red[e] = make_float2(run_mn, run_mx);
+      epi_sync();
+      if (e == 0 && lane == 0) {
+        float mn = 0.0f, mx = 0.0f;
+        for (int i = 0; i < kEpiWarps; ++i) {
+          mn = fminf(mn, red[i].x);
+          mx = fmaxf(mx, red[i].y);
+        }
+        args.minmax[blockIdx.x] = make_float2(mn, mx);
+      }
     }
   }
 
@@ -409,47 +555,108 @@ static int sm_count() {
   return n > 0 ? n : 148;
 }
 
+// Row-major 32-bit matrix [M, N] -> tensor map with 32x32 boxes and the
+// 128-byte swizzle (the epilogue's shared-memory staging layout).
+static int make_out_tmap(CUtensorMap* map, void* base, size_t M, size_t N, bool is_float) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) {
+    set_error("cuTensorMapEncodeTiled unavailable from the driver");
+    return ICX_ERR_CUDA;
+  }
+  cuuint64_t dims[2] = {(cuuint64_t)N, (cuuint64_t)M};
+  cuuint64_t strides[1] = {(cuuint64_t)N * 4};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, is_float ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_INT32,
+                  2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled (output) failed (%d) M=%zu N=%zu", (int)r, M, N);
+    return ICX_ERR_CUDA;
+  }
+  return ICX_OK;
+}
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
 template <int BN, int EPI>
 static int launch_tc(cudaStream_t s, const void* a, bool a_signed, const void* bt,
                      bool b_signed, const GemmArgs& args) {
   using C = Cfg<BN>;
-  CUtensorMap ta, tb;
+  CUtensorMap ta, tb, tout;
   int rc = make_tmap(&ta, a, (size_t)args.M, (size_t)args.K, kBM);
   if (rc) return rc;
   rc = make_tmap(&tb, bt, (size_t)args.N, (size_t)args.K, BN);
   if (rc) return rc;
-  auto kern = qgemm_tcgen05_kernel<BN, EPI>;
+  // TMA stores need a 16-byte aligned base and a row pitch multiple of 16 B
+  const int tma_store = (args.N % 4 == 0) && aligned16(args.out);
+  if (tma_store) {
+    rc = make_out_tmap(&tout, args.out, (size_t)args.M, (size_t)args.N, EPI != kEpiS32);
+    if (rc) return rc;
+  } else {
+    memset(&tout, 0, sizeof(tout));
+  }
+  const int vec_cols = (args.N % 4 == 0) && aligned16(args.colsum) &&
+                       (args.w_scale == nullptr || !args.w_scale_per_col || aligned16(args.w_scale)) &&
+                       (args.bias == nullptr || aligned16(args.bias));
+  auto kern = args.b_zp ? (args.bias ? qgemm_tcgen05_kernel<BN, EPI, true, true>
+                                      : qgemm_tcgen05_kernel<BN, EPI, true, false>)
+                        : (args.bias ? qgemm_tcgen05_kernel<BN, EPI, false, true>
+                                     : qgemm_tcgen05_kernel<BN, EPI, false, false>);
   ICX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 C::kSmemBytes));
   const int ntiles = ((args.M + kBM - 1) / kBM) * ((args.N + BN - 1) / BN);
   int grid = sm_count();
   if (ntiles < grid) grid = ntiles;
   const uint32_t idesc = idesc_i8(kBM, BN, a_signed, b_signed);
-  kern<<<grid, kThreads, C::kSmemBytes, s>>>(ta, tb, args, idesc);
+  kern<<<grid, kThreads, C::kSmemBytes, s>>>(ta, tb, tout, args, idesc, tma_store, vec_cols);
   ICX_LAUNCH_CHECK();
   return ICX_OK;
+}
+
+// Which kernel runs a GEMM and with how many CTAs.
+struct GemmPlan {
+  int bn;     // 128 / 256 for the tensor-core kernel, 0 for the SIMT kernel
+  int grid;   // CTAs (tensor-core path)
+};
+
+static GemmPlan plan_gemm(const GemmArgs& args, const void* a, const void* bt) {
+  GemmPlan p{0, 0};
+  const bool tma_ok = (args.K % 16 == 0) && args.K > 0 &&
+                      ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(bt)) & 15) == 0;
+  if (!tma_ok) return p;
+  // narrow tiles when the wide ones would leave most SMs idle
+  const long tiles256 = (long)((args.M + kBM - 1) / kBM) * ((args.N + 255) / 256);
+  p.bn = (args.N <= 128 || tiles256 < sm_count()) ? 128 : 256;
+  const long tiles = (long)((args.M + kBM - 1) / kBM) * ((args.N + p.bn - 1) / p.bn);
+  p.grid = (int)(tiles < sm_count() ? tiles : sm_count());
+  return p;
+}
+
+// Number of (min, max) partials a fused GEMM writes for its output.
+static int gemm_grid(const GemmArgs& args, const void* a, const void* bt) {
+  const GemmPlan p = plan_gemm(args, a, bt);
+  if (p.bn) return p.grid;
+  return dql_minmax_partials((size_t)args.M * args.N);
 }
 
 template <int EPI>
 static int launch_gemm(cudaStream_t s, const void* a, bool a_signed,
                        const void* bt, bool b_signed, const GemmArgs& args) {
   if (args.M == 0 || args.N == 0) return ICX_OK;
-  const bool tma_ok = (args.K % 16 == 0) && args.K > 0 &&
-                      ((reinterpret_cast<uintptr_t>(a) |
-                        reinterpret_cast<uintptr_t>(bt)) & 15) == 0;
-  if (tma_ok) {
-    // narrow tiles when the wide ones would leave most SMs idle
-    const long tiles256 = (long)((args.M + kBM - 1) / kBM) * ((args.N + 255) / 256);
-    if (tiles256 >= sm_count() || args.N <= 128)
-      return args.N <= 128 ? launch_tc<128, EPI>(s, a, a_signed, bt, b_signed, args)
-                           : launch_tc<256, EPI>(s, a, a_signed, bt, b_signed, args);
-    return launch_tc<128, EPI>(s, a, a_signed, bt, b_signed, args);
-  }
+  const GemmPlan p = plan_gemm(args, a, bt);
+  if (p.bn == 256) return launch_tc<256, EPI>(s, a, a_signed, bt, b_signed, args);
+  if (p.bn == 128) return launch_tc<128, EPI>(s, a, a_signed, bt, b_signed, args);
   const size_t total = (size_t)args.M * args.N;
   const int threads = 256;
   const size_t blocks = (total + threads - 1) / threads;
-  qgemm_simt_kernel<EPI><<<(unsigned)blocks, threads, 0, s>>>(a, a_signed, bt, b_signed, args);
+  GemmArgs g = args;
+  g.minmax = nullptr;
+  qgemm_simt_kernel<EPI><<<(unsigned)blocks, threads, 0, s>>>(a, a_signed, bt, b_signed, g);
   ICX_LAUNCH_CHECK();
+  if (EPI != kEpiS32 && args.minmax)
+    return launch_dql_minmax(s, static_cast<const float*>(args.out), total, args.minmax);
   return ICX_OK;
 }
 
@@ -591,7 +798,7 @@ extern "C" int icx_quant_linear(void* stream, const uint8_t* d_q,
                                 size_t N, const float* d_w_scale,
                                 int w_scale_per_col, const int8_t* d_b_zp,
                                 int b_zp_per_col, const float* d_bias, int gelu,
-                                float* d_out) {
+                                float* d_out, float* d_minmax, int* n_minmax) {
   ICX_REQUIRE(M < (1u << 31) && N < (1u << 30) && K < (1u << 30),
               "QuantLinear: shape too large");
   if (M == 0 || N == 0) return ICX_OK;
@@ -608,6 +815,8 @@ extern "C" int icx_quant_linear(void* stream, const uint8_t* d_q,
   g.a_scale = d_a_scale; g.w_scale = d_w_scale; g.w_scale_per_col = w_scale_per_col;
   g.bias = d_bias;
   g.out = d_out;
+  g.minmax = reinterpret_cast<float2*>(d_minmax);
+  if (n_minmax) *n_minmax = gemm_grid(g, d_q, d_wt);
   cudaStream_t s = as_stream(stream);
   return gelu ? launch_gemm<kEpiGelu>(s, d_q, false, d_wt, true, g)
               : launch_gemm<kEpiF32>(s, d_q, false, d_wt, true, g);

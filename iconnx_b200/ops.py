@@ -14,6 +14,7 @@ computation runs in libiconnx_b200.so.
 
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass
 
 import torch
@@ -174,11 +175,28 @@ def prepare_weight(b: torch.Tensor) -> PreparedWeight:
     return PreparedWeight(bt, colsum, K, N, b.dtype)
 
 
+class MinMaxPartials:
+    """(min, max) partials of a tensor written by its producer kernel."""
+
+    def __init__(self, device):
+        self.buf = torch.empty((_lib.ICX_MAX_MINMAX_PARTIALS, 2), dtype=torch.float32, device=device)
+        self.count = ctypes.c_int(0)
+
+    @property
+    def n(self) -> int:
+        return int(self.count.value)
+
+
 def quant_linear(q: torch.Tensor, a_scale: torch.Tensor, a_zp: torch.Tensor, w: PreparedWeight,
                  w_scale: torch.Tensor, bias: torch.Tensor | None = None,
                  b_zp: torch.Tensor | None = None, rowsum: torch.Tensor | None = None,
-                 gelu: bool = False, out: torch.Tensor | None = None) -> torch.Tensor:
-    """Fused MatMulInteger -> Cast -> Mul(a_scale*w_scale) -> Add(bias) [-> GELU]."""
+                 gelu: bool = False, out: torch.Tensor | None = None,
+                 minmax: "MinMaxPartials | None" = None) -> torch.Tensor:
+    """Fused MatMulInteger -> Cast -> Mul(a_scale*w_scale) -> Add(bias) [-> GELU].
+
+    With ``minmax`` the kernel also records (min, max) partials of the output
+    for a following :func:`gpu_dynamic_quantize_from_partials`.
+    """
     K = q.shape[-1]
     M = q.numel() // K
     if K != w.K or w.dtype != torch.int8:
@@ -189,17 +207,48 @@ def quant_linear(q: torch.Tensor, a_scale: torch.Tensor, a_zp: torch.Tensor, w: 
     per_col_z = int(b_zp is not None and b_zp.numel() > 1)
     check(_lib.load().icx_quant_linear(
         _stream(q), _ptr(q), _ptr(a_scale), _ptr(a_zp), _ptr(rowsum), _ptr(w.bt), _ptr(w.colsum),
-        M, K, w.N, _ptr(w_scale), per_col_s, _ptr(b_zp), per_col_z, _ptr(bias), int(gelu), _ptr(out)))
+        M, K, w.N, _ptr(w_scale), per_col_s, _ptr(b_zp), per_col_z, _ptr(bias), int(gelu), _ptr(out),
+        None if minmax is None else minmax.buf.data_ptr(),
+        None if minmax is None else ctypes.byref(minmax.count)))
+    return out
+
+
+def gpu_dynamic_quantize_from_partials(x: torch.Tensor, minmax: MinMaxPartials,
+                                       row_len: int | None = None):
+    """DynamicQuantizeLinear whose min/max scan was done by x's producer."""
+    x = _cuda(x, "DynamicQuantizeLinear")
+    if x.dtype != torch.float32:
+        raise IcxError(-1, f"DynamicQuantizeLinear: input must be Float32, got {_name(x.dtype)}")
+    n = x.numel()
+    y = torch.empty(x.shape, dtype=torch.uint8, device=x.device)
+    scale = torch.empty((), dtype=torch.float32, device=x.device)
+    zp = torch.empty((), dtype=torch.uint8, device=x.device)
+    rows = None
+    if row_len is not None:
+        rows = torch.empty(n // row_len, dtype=torch.int32, device=x.device)
+    check(_lib.load().icx_dql_quantize_f32_u8(_stream(x), _ptr(x), n, minmax.buf.data_ptr(), minmax.n,
+                                              _ptr(y), _ptr(scale), _ptr(zp), _ptr(rows), row_len or 0))
+    out = [y, scale, zp]
+    if rows is not None:
+        out.append(rows)
     return out
 
 
 def dynamic_quant_linear(x: torch.Tensor, w: PreparedWeight, w_scale: torch.Tensor,
                          bias: torch.Tensor | None = None, b_zp: torch.Tensor | None = None,
-                         gelu: bool = False):
-    """DQL(x) followed by the fused quantised Linear; returns (out, y, scale, zp)."""
+                         gelu: bool = False, x_minmax: MinMaxPartials | None = None,
+                         out_minmax: MinMaxPartials | None = None):
+    """DQL(x) followed by the fused quantised Linear; returns (out, y, scale, zp).
+
+    ``x_minmax``: partials of x from its producer (skips the min/max pass);
+    ``out_minmax``: collect partials of the output for the next DQL.
+    """
     K = x.shape[-1]
-    outs = gpu_dynamic_quantize_linear(x, row_len=K if b_zp is not None else None)
+    if x_minmax is not None:
+        outs = gpu_dynamic_quantize_from_partials(x, x_minmax, row_len=K if b_zp is not None else None)
+    else:
+        outs = gpu_dynamic_quantize_linear(x, row_len=K if b_zp is not None else None)
     y, s, z = outs[:3]
     rows = outs[3] if b_zp is not None else None
-    out = quant_linear(y, s, z, w, w_scale, bias, b_zp, rows, gelu)
+    out = quant_linear(y, s, z, w, w_scale, bias, b_zp, rows, gelu, minmax=out_minmax)
     return out, y, s, z

@@ -51,6 +51,11 @@ extern "C" {
 #define ICX_DEVICE_TIMEOUT_MMA 0x102
 #define ICX_DEVICE_TIMEOUT_EPILOGUE 0x103
 
+/* Upper bound on the (min, max) partial pairs a producer writes for a
+ * following DynamicQuantizeLinear (icx_quant_linear d_minmax, and the
+ * partials icx_dql_quantize_f32_u8 consumes). */
+#define ICX_MAX_MINMAX_PARTIALS 1184
+
 /* ---- element types ----------------------------------------------------- */
 #define ICX_U8 0
 #define ICX_S8 1
@@ -85,6 +90,16 @@ ICX_API size_t icx_dql_workspace_bytes(size_t n);
 ICX_API int icx_dql_f32_u8(void* stream, const float* d_x, size_t n, uint8_t* d_y,
                    float* d_scale, uint8_t* d_zp, int32_t* d_rowsum,
                    size_t row_len, void* d_workspace, size_t workspace_bytes);
+
+/* The quantise pass of DynamicQuantizeLinear alone, for an x whose producer
+ * already wrote (min, max) partials of x (d_minmax: n_minmax float pairs,
+ * each seeded with 0 and NaN-skipping, e.g. icx_quant_linear's d_minmax).
+ * Same outputs and bit-exact results as icx_dql_f32_u8; saves one full read
+ * of x.  Replaces the same reference function as icx_dql_f32_u8. */
+ICX_API int icx_dql_quantize_f32_u8(void* stream, const float* d_x, size_t n,
+                                    const float* d_minmax, int n_minmax,
+                                    uint8_t* d_y, float* d_scale, uint8_t* d_zp,
+                                    int32_t* d_rowsum, size_t row_len);
 
 /* ======================================================================== *
  * Weight preparation for MatMulInteger.
@@ -140,6 +155,10 @@ ICX_API int icx_matmul_integer_prepared(void* stream, const void* d_a, int a_typ
  * outputs; wt/colsum: prepared weight; w_scale: 1 or N floats; b_zp: NULL,
  * 1 or N s8 values; bias: N floats (or NULL); out: f32 [M, N].
  * The s32 accumulator never leaves the SM: it lives in tensor memory.
+ * d_minmax (nullable, room for ICX_MAX_MINMAX_PARTIALS float pairs): the
+ * kernel also writes (min, max) partials of `out` (seeded with 0, NaN
+ * skipped) so a following DynamicQuantizeLinear needs only its quantise
+ * pass; *n_minmax receives how many pairs were written.
  * ======================================================================== */
 ICX_API int icx_quant_linear(void* stream, const uint8_t* d_q, const float* d_a_scale,
                      const uint8_t* d_a_zp, const int32_t* d_rowsum_q,
@@ -147,7 +166,7 @@ ICX_API int icx_quant_linear(void* stream, const uint8_t* d_q, const float* d_a_
                      size_t K, size_t N, const float* d_w_scale,
                      int w_scale_per_col, const int8_t* d_b_zp,
                      int b_zp_per_col, const float* d_bias, int gelu,
-                     float* d_out);
+                     float* d_out, float* d_minmax, int* n_minmax);
 
 /* ======================================================================== *
  * DequantizeLinear: y = (f32(x) - f32(zp)) * scale, per tensor or per axis.

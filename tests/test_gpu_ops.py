@@ -292,3 +292,43 @@ def test_ffn_block_stagewise():
     np.testing.assert_array_equal(host(y2), ry2)
     assert host(s2).item() == rs2 and host(z2).item() == rz2
     np.testing.assert_array_equal(host(out).view(np.uint32), rout.view(np.uint32))
+
+
+@pytest.mark.parametrize("M,K,N,gelu,per_col", [(4096, 768, 3072, True, False), (300, 64, 77, False, False),
+                                                (512, 768, 768, False, True), (5, 3, 9, False, False)])
+def test_producer_fused_minmax_then_quantize(M, K, N, gelu, per_col):
+    """GEMM epilogue writes (min, max) partials; the next DQL's quantise pass
+    alone must equal a full DQL of the same tensor (and the oracle)."""
+    x = synth.normal((M, K), 1.0, 21)
+    w = synth.int8_uniform((K, N), 22)
+    bias = synth.normal((N,), 0.02, 23)
+    ws = synth.uniform_f32((N,), 0.005, 0.02, 24) if per_col else np.array([0.01], np.float32)
+    bz = synth.int8_uniform((N,), 25, -8, 8) if per_col else None
+    pw = ops.prepare_weight(cu(w))
+    mm = ops.MinMaxPartials(DEV)
+    h, *_ = ops.dynamic_quant_linear(cu(x), pw, cu(ws), cu(bias), None if bz is None else cu(bz),
+                                     gelu, out_minmax=mm)
+    assert 1 <= mm.n <= 1184
+    y1, s1, z1 = ops.gpu_dynamic_quantize_from_partials(h, mm)
+    y2, s2, z2 = ops.gpu_dynamic_quantize_linear(h)
+    oy, os_, oz = oracle.dynamic_quantize_linear(host(h))
+    np.testing.assert_array_equal(host(y1), oy)
+    np.testing.assert_array_equal(host(y2), oy)
+    assert host(s1).item() == host(s2).item() == os_ and host(z1).item() == oz
+
+
+def test_ffn_block_fused_chain_bit_exact():
+    """Config 2 with the producer-fused DQL2: DQL2 and GEMM2 stages bit-exact."""
+    M = 4096
+    x = synth.normal((M, 768), 1.0, 0)
+    w1, w2 = synth.int8_uniform((768, 3072), 1), synth.int8_uniform((3072, 768), 3)
+    b1, b2 = synth.normal((3072,), 0.02, 2), synth.normal((768,), 0.02, 102)
+    ws = np.array([0.01], np.float32)
+    p1, p2 = ops.prepare_weight(cu(w1)), ops.prepare_weight(cu(w2))
+    mm = ops.MinMaxPartials(DEV)
+    h, *_ = ops.dynamic_quant_linear(cu(x), p1, cu(ws), cu(b1), gelu=True, out_minmax=mm)
+    out, y2, s2, z2 = ops.dynamic_quant_linear(h, p2, cu(ws), cu(b2), x_minmax=mm)
+    rout, ry2, rs2, rz2, _ = oracle.quant_linear(host(h), w2, ws, b2, None, False, threads=8)
+    np.testing.assert_array_equal(host(y2), ry2)
+    assert host(s2).item() == rs2 and host(z2).item() == rz2
+    np.testing.assert_array_equal(host(out).view(np.uint32), rout.view(np.uint32))
