@@ -21,6 +21,8 @@
 // result.  Otherwise (about 0.02% of random inputs, and all exact ties) the
 // element takes the f64 division path.  Non-finite values and scales whose
 // reciprocal is not a normal f32 also take the f64 path.
+#include <mutex>
+
 #include "capi.cuh"
 #include "common.cuh"
 
@@ -305,6 +307,84 @@ extern "C" int icx_dql_quantize_f32_u8(void* stream, const float* d_x, size_t n,
   dql_quantize_kernel<<<(int)qb, kQuantThreads, 0, s>>>(
       d_x, n, reinterpret_cast<const float2*>(d_minmax), n_minmax, d_y, d_scale, d_zp,
       d_rowsum, row_len ? row_len : 1, vec16);
+  ICX_LAUNCH_CHECK();
+  return ICX_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free DynamicQuantizeLinear.
+//
+// Some callers cannot allocate device memory at the moment they quantise:
+// code running inside a fixed memory budget that was reserved up front, a
+// host runtime whose allocator may not be re-entered from its execution
+// thread, or an embedder that forbids cudaMalloc after start-up because
+// cudaMalloc can synchronise the device.  For them this entry point keeps its
+// scratch (the per-block (min, max) partials) in a file-scope device array
+// instead of a caller-provided workspace.
+//
+// The array holds ICX_MAX_MINMAX_PARTIALS pairs (9472 bytes) and stays
+// resident on every GPU that loads this library until the process exits.
+// Nothing in it needs clearing between calls: every block of the min/max pass
+// overwrites its own slot before the quantise pass reads it.  All calls on a
+// device share the one array, so two calls whose kernels overlap on the GPU
+// (different streams, no ordering between them) race on it.
+static __device__ __align__(256) float2 g_dql_noalloc_scratch[ICX_MAX_MINMAX_PARTIALS];
+
+namespace icx {
+namespace {
+constexpr int kNoallocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+float2* g_noalloc_ptr[kNoallocMaxDevices] = {};
+
+// Device address of the scratch array on the current device.  The symbol's
+// name in host code is only a host-side handle; the real address comes from
+// cudaGetSymbolAddress, looked up once per device with that device current.
+int noalloc_scratch(float2** out) {
+  int dev = 0;
+  ICX_CUDA(cudaGetDevice(&dev));
+  ICX_REQUIRE(dev >= 0 && dev < kNoallocMaxDevices, "DynamicQuantizeLinear: device %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    ICX_CUDA(cudaGetSymbolAddress(&p, g_dql_noalloc_scratch));
+    g_noalloc_ptr[dev] = static_cast<float2*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return ICX_OK;
+}
+}  // namespace
+}  // namespace icx
+
+extern "C" int icx_dql_f32_u8_noalloc(void* stream, const float* d_x, size_t n,
+                                      uint8_t* d_y, float* d_scale, uint8_t* d_zp,
+                                      int32_t* d_rowsum, size_t row_len) {
+  ICX_REQUIRE(n <= ICX_DQL_NOALLOC_MAX_N,
+              "DynamicQuantizeLinear (no-alloc): n = %zu exceeds the maximum of %llu elements",
+              n, (unsigned long long)ICX_DQL_NOALLOC_MAX_N);
+  ICX_REQUIRE(d_scale && d_zp, "DynamicQuantizeLinear: null scale/zp output");
+  ICX_REQUIRE(n == 0 || (d_x && d_y), "DynamicQuantizeLinear: null x or y");
+  ICX_REQUIRE(d_rowsum == nullptr || (row_len > 0 && n % row_len == 0),
+              "DynamicQuantizeLinear: row_len %zu must divide n %zu", row_len, n);
+  const int blocks = minmax_blocks(n);
+  ICX_REQUIRE(blocks <= ICX_MAX_MINMAX_PARTIALS,
+              "DynamicQuantizeLinear (no-alloc): %d partials exceed the scratch of %d", blocks,
+              ICX_MAX_MINMAX_PARTIALS);
+  float2* scratch = nullptr;
+  int rc = noalloc_scratch(&scratch);
+  if (rc) return rc;
+  cudaStream_t s = as_stream(stream);
+  const size_t nrows = d_rowsum ? n / row_len : 0;
+  dql_minmax_kernel<<<blocks, kMinmaxThreads, 0, s>>>(d_x, n, scratch, d_rowsum, nrows);
+  ICX_LAUNCH_CHECK();
+  const bool aligned = ((reinterpret_cast<uintptr_t>(d_x) |
+                         reinterpret_cast<uintptr_t>(d_y)) & 15) == 0;
+  const int vec16 = aligned && (d_rowsum == nullptr || row_len % 4 == 0);
+  size_t work = vec16 ? n / 16 : n;
+  size_t qb = (work + kQuantThreads - 1) / kQuantThreads;
+  if (qb < 1) qb = 1;
+  if (qb > 148 * 8) qb = 148 * 8;
+  dql_quantize_kernel<<<(int)qb, kQuantThreads, 0, s>>>(
+      d_x, n, scratch, blocks, d_y, d_scale, d_zp, d_rowsum, row_len ? row_len : 1, vec16);
   ICX_LAUNCH_CHECK();
   return ICX_OK;
 }

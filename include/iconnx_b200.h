@@ -91,6 +91,25 @@ ICX_API int icx_dql_f32_u8(void* stream, const float* d_x, size_t n, uint8_t* d_
                    float* d_scale, uint8_t* d_zp, int32_t* d_rowsum,
                    size_t row_len, void* d_workspace, size_t workspace_bytes);
 
+/* Allocation-free DynamicQuantizeLinear.  No counterpart in the reference
+ * engine.  For callers that must not allocate device memory while they run
+ * (a fixed memory budget reserved at start-up, an allocator that may not be
+ * re-entered from the calling thread, or a host that forbids cudaMalloc
+ * because it can synchronise the device): same inputs, outputs and bit-exact
+ * results as icx_dql_f32_u8, but the scratch lives in a 9472-byte array
+ * compiled into this library (resident on each GPU that loads it until the
+ * process exits) instead of a caller workspace.  Calls no allocator.
+ * Limit: n <= ICX_DQL_NOALLOC_MAX_N, larger n is rejected with
+ * ICX_ERR_INVALID.  The first call on a device looks up the array's device
+ * address (cudaGetSymbolAddress); make that first call before any stream
+ * capture.  All calls on a device share the array: calls whose kernels may
+ * overlap on the GPU (e.g. unordered streams) race and must be serialised by
+ * the caller. */
+#define ICX_DQL_NOALLOC_MAX_N (1ull << 32)
+ICX_API int icx_dql_f32_u8_noalloc(void* stream, const float* d_x, size_t n,
+                                   uint8_t* d_y, float* d_scale, uint8_t* d_zp,
+                                   int32_t* d_rowsum, size_t row_len);
+
 /* The quantise pass of DynamicQuantizeLinear alone, for an x whose producer
  * already wrote (min, max) partials of x (d_minmax: n_minmax float pairs,
  * each seeded with 0 and NaN-skipping, e.g. icx_quant_linear's d_minmax).
