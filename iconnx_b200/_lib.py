@@ -15,7 +15,7 @@ HEADER = os.path.join(os.path.dirname(HERE), "include", "iconnx_b200.h")
 
 ICX_OK = 0
 ICX_MAX_MINMAX_PARTIALS = 1184
-ICX_U8, ICX_S8, ICX_S32, ICX_F32 = 0, 1, 2, 3
+ICX_U8, ICX_S8, ICX_S32, ICX_F32, ICX_S64, ICX_BOOL = 0, 1, 2, 3, 4, 5
 
 _vp, _sz, _i = ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int
 
@@ -36,6 +36,20 @@ PROTOTYPES = {
     "icx_dql_f32_u8_noalloc": (_i, [_vp, _vp, _sz, _vp, _vp, _vp, _vp, _sz]),
     "icx_dql_quantize_f32_u8": (_i, [_vp, _vp, _sz, _vp, _i, _vp, _vp, _vp, _vp, _sz]),
     "icx_dequantize_linear": (_i, [_vp, _vp, _i, _sz, _sz, _sz, _vp, _sz, _vp, _vp]),
+    "icx_matmul_integer_rowsum": (_i, [_vp, _vp, _i, _sz, _sz, _vp]),
+    "icx_engine_create": (_vp, [_i]),
+    "icx_engine_destroy": (None, [_vp]),
+    "icx_engine_add_input": (_i, [_vp, ctypes.c_char_p, _i, _i, _vp]),
+    "icx_engine_add_initializer": (_i, [_vp, ctypes.c_char_p, _i, _i, _vp, _vp]),
+    "icx_engine_add_node": (_i, [_vp, ctypes.c_char_p, ctypes.c_char_p, _i, _vp, _i, _vp, _i, _vp]),
+    "icx_engine_run": (_i, [_vp, _i, _vp, _vp, _vp, _vp, _vp, _i, _vp]),
+    "icx_engine_output_info": (_i, [_vp, ctypes.c_char_p, _vp, _vp, _vp]),
+    "icx_engine_output_copy": (_i, [_vp, ctypes.c_char_p, _vp, _sz]),
+    "icx_engine_plan": (ctypes.c_char_p, [_vp]),
+    "icx_engine_set_cuda_graphs": (_i, [_vp, _i]),
+    "icx_engine_kernel_launches": (_i, [_vp]),
+    "icx_engine_replay": (_i, [_vp]),
+    "icx_engine_stream": (_vp, [_vp]),
 }
 
 _lib = None

@@ -1,0 +1,38 @@
+// Internal launch helpers shared by the engine (not part of the C ABI).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <vector>
+
+#include "../../include/iconnx_b200.h"
+
+namespace icx {
+
+constexpr int kMaxRank = 6;
+enum BinaryOp { kAdd = 0, kSub = 1, kMul = 2, kDiv = 3 };
+
+size_t dtype_size(int t);
+
+int launch_gather_rows(cudaStream_t s, const float* table, int64_t rows, const int64_t* idx,
+                       size_t n, size_t D, float* out, int* err);
+int launch_binary(cudaStream_t s, int op, const float* a, const std::vector<int64_t>& ashape,
+                  const float* b, const std::vector<int64_t>& bshape, float* out,
+                  const std::vector<int64_t>& oshape);
+int layernorm_partials(size_t rows);
+int launch_layernorm(cudaStream_t s, const float* x, const float* gamma, const float* beta,
+                     float* y, size_t rows, size_t D, float eps, float* minmax, int* n_minmax);
+int launch_softmax(cudaStream_t s, const float* x, float* y, size_t rows, size_t D);
+int launch_transpose(cudaStream_t s, const void* x, int elem_bytes,
+                     const std::vector<int64_t>& in_shape, const std::vector<int64_t>& perm,
+                     void* y);
+int launch_cast(cudaStream_t s, const void* x, int from, void* y, int to, size_t n);
+int launch_erf(cudaStream_t s, const float* x, float* y, size_t n);
+int launch_gelu(cudaStream_t s, const float* x, float* y, size_t n);
+
+// dql.cu
+int dql_minmax_partials(size_t n);
+int launch_dql_minmax(cudaStream_t s, const float* x, size_t n, float2* partials);
+
+}  // namespace icx

@@ -821,3 +821,22 @@ extern "C" int icx_quant_linear(void* stream, const uint8_t* d_q,
   return gelu ? launch_gemm<kEpiGelu>(s, d_q, false, d_wt, true, g)
               : launch_gemm<kEpiF32>(s, d_q, false, d_wt, true, g);
 }
+
+extern "C" int icx_matmul_integer_rowsum(void* stream, const void* d_a, int a_type, size_t M,
+                                         size_t K, int32_t* d_rowsum) {
+  ICX_REQUIRE(is_8bit(a_type), "MatMulInteger: input a must be Int8 or UInt8");
+  ICX_REQUIRE(M < (1u << 31) && K < (1u << 30), "MatMulInteger: shape too large");
+  if (M == 0) return ICX_OK;
+  ICX_REQUIRE(d_rowsum && (K == 0 || d_a), "MatMulInteger: null pointer");
+  cudaStream_t s = as_stream(stream);
+  if (K == 0) {
+    ICX_CUDA(cudaMemsetAsync(d_rowsum, 0, M * 4, s));
+    return ICX_OK;
+  }
+  const int threads = 256;
+  const size_t blocks = (M * 32 + threads - 1) / threads;
+  rowsum_kernel<<<(unsigned)blocks, threads, 0, s>>>(static_cast<const uint8_t*>(d_a),
+                                                     a_type == ICX_S8, (int)M, (int)K, d_rowsum);
+  ICX_LAUNCH_CHECK();
+  return ICX_OK;
+}

@@ -1,0 +1,179 @@
+"""GpuGraphExecutor: host-side mirror of the reference's public executor API
+(src/cuda/inference/mod.rs:222-659) over the C++ engine in
+libiconnx_b200.so (include/iconnx_b200.h, icx_engine_*).
+
+    ex = GpuGraphExecutor.new()            # or GpuGraphExecutor.from_model(model)
+    ex.add_input("x", [32, 128, 768])
+    ex.add_initializer("W", np_int8_array)
+    ex.add_node("n0", "DynamicQuantizeLinear", ["x"], ["q", "s", "z"])
+    ...
+    outs = ex.run({"x": x}, ["y"])         # host arrays in, host arrays out
+
+As in the reference, lowering happens lazily on the first run; a run whose
+input shape conflicts with a declared static dimension raises
+``IcxError`` with status ICX_ERR_SHAPE_MISMATCH (the reference's
+CudaError::InputShapeMismatch).  One executor per thread: the reference's is
+``!Sync`` and so is this one.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+
+from . import _lib
+from ._lib import IcxError, check
+
+_NP2ICX = {np.dtype(np.uint8): _lib.ICX_U8, np.dtype(np.int8): _lib.ICX_S8,
+           np.dtype(np.int32): _lib.ICX_S32, np.dtype(np.float32): _lib.ICX_F32,
+           np.dtype(np.int64): _lib.ICX_S64, np.dtype(np.bool_): _lib.ICX_BOOL}
+_ICX2NP = {v: k for k, v in _NP2ICX.items()}
+_DT_NAMES = {"float32": np.float32, "uint8": np.uint8, "int8": np.int8, "int32": np.int32,
+             "int64": np.int64, "bool": np.bool_}
+
+
+class _Attr(ctypes.Structure):
+    _fields_ = [("name", ctypes.c_char_p), ("kind", ctypes.c_int), ("i", ctypes.c_int64),
+                ("f", ctypes.c_float), ("ints", ctypes.POINTER(ctypes.c_int64)),
+                ("floats", ctypes.POINTER(ctypes.c_float)), ("n", ctypes.c_int),
+                ("s", ctypes.c_char_p)]
+
+
+def _strs(items):
+    arr = (ctypes.c_char_p * max(len(items), 1))()
+    for i, s in enumerate(items):
+        arr[i] = s.encode() if s else b""
+    return arr
+
+
+class GpuGraphExecutor:
+    """One GPU graph executor (one CUDA stream on ``device``)."""
+
+    def __init__(self, device: int = 0):
+        L = _lib.load()
+        self._L = L
+        self._h = L.icx_engine_create(device)
+        if not self._h:
+            raise IcxError(-2, "icx_engine_create failed: " + L.icx_last_error().decode())
+        self.device = device
+        self._keep = []
+
+    @classmethod
+    def new(cls, device: int = 0) -> "GpuGraphExecutor":
+        return cls(device)
+
+    @classmethod
+    def from_model(cls, model, device: int = 0) -> "GpuGraphExecutor":
+        """Builds an executor from an OnnxModel (iconnx_b200.onnx.OnnxParser),
+        like GpuGraphExecutor::from_model (src/cuda/inference/mod.rs:246-267)."""
+        ex = cls(device)
+        for name, (dtype, shape) in model.input_shapes().items():
+            ex.add_input(name, shape, dtype)
+        for name, arr in model.extract_weights().items():
+            ex.add_initializer(name, arr)
+        for i, node in enumerate(model.nodes):
+            ex.add_node(node.name or f"n{i}", node.op_type, node.inputs, node.outputs, node.attrs)
+        return ex
+
+    def __del__(self):
+        h = getattr(self, "_h", None)
+        if h:
+            self._L.icx_engine_destroy(h)
+            self._h = None
+
+    # ------------------------------------------------------------- builder
+    def add_input(self, name: str, shape, dtype=np.float32) -> None:
+        dims = (ctypes.c_int64 * max(len(shape), 1))(*[int(d) if d is not None else -1 for d in shape])
+        check(self._L.icx_engine_add_input(self._h, name.encode(), _NP2ICX[np.dtype(dtype)],
+                                           len(shape), dims))
+
+    def add_initializer(self, name: str, array) -> None:
+        a = np.ascontiguousarray(array)
+        if a.dtype not in _NP2ICX:
+            raise IcxError(-1, f"add_initializer {name}: dtype {a.dtype} unsupported")
+        dims = (ctypes.c_int64 * max(a.ndim, 1))(*a.shape)
+        check(self._L.icx_engine_add_initializer(self._h, name.encode(), _NP2ICX[a.dtype], a.ndim,
+                                                 dims, a.ctypes.data_as(ctypes.c_void_p)))
+
+    def add_node(self, name: str, op_type: str, inputs, outputs, attributes=None) -> None:
+        attrs = attributes or {}
+        arr = (_Attr * max(len(attrs), 1))()
+        keep = []
+        for k, (key, v) in enumerate(attrs.items()):
+            a = arr[k]
+            a.name = key.encode()
+            if isinstance(v, bool) or isinstance(v, (int, np.integer)):
+                a.kind, a.i = 1, int(v)
+            elif isinstance(v, (float, np.floating)):
+                a.kind, a.f = 2, float(v)
+            elif isinstance(v, str):
+                a.kind, a.s = 4, v.encode()
+            else:
+                vals = list(v)
+                if vals and isinstance(vals[0], (float, np.floating)):
+                    buf = (ctypes.c_float * len(vals))(*vals)
+                    a.kind, a.floats = 5, buf
+                else:
+                    buf = (ctypes.c_int64 * max(len(vals), 1))(*[int(x) for x in vals])
+                    a.kind, a.ints = 3, buf
+                a.n = len(vals)
+                keep.append(buf)
+        check(self._L.icx_engine_add_node(self._h, (name or "").encode(), op_type.encode(),
+                                          len(inputs), _strs(inputs), len(outputs), _strs(outputs),
+                                          len(attrs), arr))
+
+    # ----------------------------------------------------------------- run
+    def run(self, inputs: dict, outputs) -> dict:
+        """Host arrays in, host arrays out (src/cuda/inference/mod.rs:428-464)."""
+        self.run_device(inputs, outputs)
+        return {name: self.fetch(name) for name in outputs}
+
+    def run_device(self, inputs: dict, outputs) -> None:
+        """Runs the graph; the outputs stay on the GPU until :meth:`fetch`."""
+        names = list(inputs)
+        arrs = [np.ascontiguousarray(inputs[n]) for n in names]
+        for n, a in zip(names, arrs):
+            if a.dtype not in _NP2ICX:
+                raise IcxError(-1, f"run: input '{n}' dtype {a.dtype} unsupported")
+        k = len(names)
+        dtypes = (ctypes.c_int * max(k, 1))(*[_NP2ICX[a.dtype] for a in arrs])
+        ranks = (ctypes.c_int * max(k, 1))(*[a.ndim for a in arrs])
+        flat = [d for a in arrs for d in a.shape]
+        dims = (ctypes.c_int64 * max(len(flat), 1))(*flat)
+        ptrs = (ctypes.c_void_p * max(k, 1))(*[a.ctypes.data for a in arrs])
+        self._inputs_alive = arrs
+        check(self._L.icx_engine_run(self._h, k, _strs(names), dtypes, ranks, dims, ptrs,
+                                     len(outputs), _strs(list(outputs))))
+
+    def fetch(self, name: str, out: np.ndarray | None = None) -> np.ndarray:
+        dt, rk = ctypes.c_int(), ctypes.c_int()
+        dims = (ctypes.c_int64 * 6)()
+        check(self._L.icx_engine_output_info(self._h, name.encode(), ctypes.byref(dt),
+                                             ctypes.byref(rk), dims))
+        shape = tuple(dims[i] for i in range(rk.value))
+        if out is None:
+            out = np.empty(shape, dtype=_ICX2NP[dt.value])
+        check(self._L.icx_engine_output_copy(self._h, name.encode(), out.ctypes.data_as(ctypes.c_void_p),
+                                             out.nbytes))
+        return out
+
+    # -------------------------------------------------------- introspection
+    def plan(self) -> list[str]:
+        """The compiled launch plan, one 'op node -> output' line per step."""
+        return [ln for ln in self._L.icx_engine_plan(self._h).decode().splitlines() if ln]
+
+    def replay(self) -> None:
+        """Re-run the compiled plan on the device-resident inputs of the last
+        run (asynchronous, on :meth:`stream`)."""
+        check(self._L.icx_engine_replay(self._h))
+
+    def stream(self) -> int:
+        """The executor's cudaStream_t as an integer handle."""
+        return int(self._L.icx_engine_stream(self._h) or 0)
+
+    def kernel_launches(self) -> int:
+        return int(self._L.icx_engine_kernel_launches(self._h))
+
+    def set_cuda_graphs(self, enabled: bool) -> None:
+        check(self._L.icx_engine_set_cuda_graphs(self._h, int(enabled)))

@@ -61,6 +61,8 @@ extern "C" {
 #define ICX_S8 1
 #define ICX_S32 2
 #define ICX_F32 3
+#define ICX_S64 4
+#define ICX_BOOL 5
 
 /* Message for the last failing call on this thread ("" if none). */
 ICX_API const char* icx_last_error(void);
@@ -200,6 +202,68 @@ ICX_API int icx_dequantize_linear(void* stream, const void* d_x, int x_type,
                           size_t outer, size_t axis_len, size_t inner,
                           const float* d_scale, size_t scale_len,
                           const void* d_zp, float* d_y);
+
+/* Row sums of an 8-bit matrix a [M, K] (the rowsum_a operand of
+ * icx_matmul_integer_prepared when b has a zero point).  Part of the
+ * MatMulInteger path replacing src/cuda/ops/quantize.rs:398-615. */
+ICX_API int icx_matmul_integer_rowsum(void* stream, const void* d_a, int a_type, size_t M,
+                                      size_t K, int32_t* d_rowsum);
+
+/* ======================================================================== *
+ * Graph executor.  Replaces GpuGraphExecutor (src/cuda/inference/mod.rs:
+ * 222-659): new (:222), add_input (:306), add_initializer (:316),
+ * add_node (:330), run (:428, host tensors in and out), with lazy lowering
+ * on the first run (:484-536) and the input-shape guard (:441-460, error
+ * ICX_ERR_SHAPE_MISMATCH).  Lowering fuses every
+ * DynamicQuantizeLinear -> MatMulInteger -> Cast -> Mul -> Add [-> GELU]
+ * chain into one tensor-core kernel.  One executor per thread (the
+ * reference's is !Sync); each owns a CUDA stream on `device`.
+ * Element types of inputs/initializers: ICX_* codes; dims are int64.
+ * ======================================================================== */
+typedef struct icx_engine icx_engine;
+
+/* Node attribute: kind 1 int (i), 2 float (f), 3 ints (ints[n]),
+ * 4 string (s), 5 floats (floats[n]). */
+typedef struct icx_attr {
+  const char* name;
+  int kind;
+  int64_t i;
+  float f;
+  const int64_t* ints;
+  const float* floats;
+  int n;
+  const char* s;
+} icx_attr;
+
+ICX_API icx_engine* icx_engine_create(int device);  /* NULL on failure */
+ICX_API void icx_engine_destroy(icx_engine* e);
+ICX_API int icx_engine_add_input(icx_engine* e, const char* name, int dtype, int rank,
+                                 const int64_t* dims);  /* dims <= 0: dynamic */
+ICX_API int icx_engine_add_initializer(icx_engine* e, const char* name, int dtype, int rank,
+                                       const int64_t* dims, const void* host_data);
+ICX_API int icx_engine_add_node(icx_engine* e, const char* name, const char* op_type, int n_in,
+                                const char* const* inputs, int n_out,
+                                const char* const* outputs, int n_attrs, const icx_attr* attrs);
+/* Runs the graph on host inputs (dims concatenated over inputs); the
+ * requested outputs stay on the device until icx_engine_output_copy. */
+ICX_API int icx_engine_run(icx_engine* e, int n_in, const char* const* names, const int* dtypes,
+                           const int* ranks, const int64_t* dims, const void* const* host,
+                           int n_out, const char* const* outputs);
+ICX_API int icx_engine_output_info(icx_engine* e, const char* name, int* dtype, int* rank,
+                                   int64_t* dims /* [6] */);
+ICX_API int icx_engine_output_copy(icx_engine* e, const char* name, void* host, size_t bytes);
+/* The compiled plan, one "op node -> output" line per launch step. */
+ICX_API const char* icx_engine_plan(icx_engine* e);
+/* Replay the compiled plan as a CUDA graph after the first run (default on). */
+ICX_API int icx_engine_set_cuda_graphs(icx_engine* e, int enabled);
+/* Re-executes the compiled plan on the inputs already on the device from the
+ * last run: enqueued on the engine's stream, no copies, no synchronisation
+ * (device-resident throughput measurement). */
+ICX_API int icx_engine_replay(icx_engine* e);
+/* The engine's CUDA stream (cudaStream_t as void*). */
+ICX_API void* icx_engine_stream(icx_engine* e);
+/* Kernel launches per run of the compiled plan. */
+ICX_API int icx_engine_kernel_launches(icx_engine* e);
 
 #ifdef __cplusplus
 }

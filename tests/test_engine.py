@@ -1,0 +1,133 @@
+"""The graph executor (GpuGraphExecutor over the C++ engine) against the CPU
+graph interpreter restating the reference's CPU GraphExecutor
+(src/graph_executor.rs:92-278), on the synthetic configuration graphs.
+
+int8 chains: bit-exact (u8/s32 and the dequantised f32); after erf-GELU
+1e-5; whole encoders (fp32 LayerNorm / softmax / attention GEMMs round
+differently on the GPU, which can move a quantised value by one step):
+5e-2 absolute on the LayerNorm-normalised hidden states.
+"""
+import numpy as np
+import pytest
+
+from iconnx_b200 import IcxError, graphs, synth
+from oracle.graph_executor import CpuGraph
+
+gpu = pytest.mark.gpu
+
+
+def both(build, *args, **kw):
+    from iconnx_b200.engine import GpuGraphExecutor
+    ex, cpu = GpuGraphExecutor.new(), CpuGraph()
+    out = build(ex, *args, **kw)
+    build(cpu, *args, **kw)
+    return ex, cpu, out
+
+
+def test_cpu_interpreter_runs_config1_chain():
+    cpu = CpuGraph()
+    out = graphs.build_linear(cpu, M=8, K=32, N=16)
+    x = synth.normal((1, 8, 32), 1.0, 0)
+    y = cpu.run({"x": x}, [out])[out]
+    assert y.shape == (1, 8, 16) and y.dtype == np.float32
+
+
+def test_engine_create_fails_cleanly_without_gpu():
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("GPU present")
+    from iconnx_b200.engine import GpuGraphExecutor
+    with pytest.raises(IcxError):
+        GpuGraphExecutor.new()
+
+
+@gpu
+def test_config1_linear_bit_exact_and_fused():
+    ex, cpu, out = both(graphs.build_linear)
+    x = synth.normal((1, 128, 768), 1.0, 0)
+    g = ex.run({"x": x}, [out])[out]
+    r = cpu.run({"x": x}, [out])[out]
+    np.testing.assert_array_equal(g.view(np.uint32), r.view(np.uint32))
+    plan = ex.plan()
+    assert any(s.startswith("QuantLinear ") for s in plan)
+    assert not any(s.startswith(("MatMulInteger", "Cast", "Mul", "Add")) for s in plan)
+    # second run replays the captured CUDA graph
+    g2 = ex.run({"x": x}, [out])[out]
+    np.testing.assert_array_equal(g2, g)
+
+
+@gpu
+def test_config2_ffn_block():
+    ex, cpu, out = both(graphs.build_ffn, batch=2, seq=128)
+    x = synth.normal((256, 768), 1.0, 0)
+    g = ex.run({"x": x}, [out])[out]
+    r = cpu.run({"x": x}, [out])[out]
+    plan = ex.plan()
+    assert any(s.startswith("QuantLinear+GELU") for s in plan)
+    assert any(s.startswith("DynamicQuantizeLinear(quantise)") for s in plan)
+    np.testing.assert_allclose(g, r, atol=2e-3, rtol=1e-4)
+
+
+@gpu
+def test_unfused_per_op_dispatch_bit_exact():
+    """MatMulInteger / DequantizeLinear reached through the per-op dispatch
+    (u8 weights with zero points, rank-3 activations), like layout.rs:978-1097."""
+    def build(g):
+        g.add_input("a", [2, 16, 64], np.uint8)
+        g.add_initializer("b", np.random.default_rng(0).integers(0, 256, (64, 40), dtype=np.uint8))
+        g.add_initializer("az", np.array(7, np.uint8))
+        g.add_initializer("bz", np.array(130, np.uint8))
+        g.add_initializer("sc", np.array(0.02, np.float32))
+        g.add_node("mmi", "MatMulInteger", ["a", "b", "az", "bz"], ["acc"])
+        g.add_node("deq", "DequantizeLinear", ["acc", "sc"], ["y"])
+        return "y"
+    ex, cpu, out = both(build)
+    a = np.random.default_rng(1).integers(0, 256, (2, 16, 64), dtype=np.uint8)
+    g = ex.run({"a": a}, [out, "acc"])
+    r = cpu.run({"a": a}, [out, "acc"])
+    np.testing.assert_array_equal(g["acc"], r["acc"])
+    np.testing.assert_array_equal(g[out], r[out])
+
+
+@gpu
+def test_shape_guard_and_dtype_errors():
+    from iconnx_b200.engine import GpuGraphExecutor
+    ex = GpuGraphExecutor.new()
+    out = graphs.build_linear(ex)
+    with pytest.raises(IcxError, match="InputShapeMismatch"):
+        ex.run({"x": np.zeros((1, 64, 768), np.float32)}, [out])
+    with pytest.raises(IcxError, match="dtype"):
+        ex.run({"x": np.zeros((1, 128, 768), np.int32)}, [out])
+
+
+@gpu
+@pytest.mark.parametrize("cfg,batch,seq", [
+    (graphs.BertConfig(layers=2), 2, 16),
+    (graphs.BertConfig(layers=1, per_channel=True, token_type=True), 2, 32),
+])
+def test_encoder_matches_cpu_interpreter(cfg, batch, seq):
+    ex, cpu, out = both(graphs.build_bert, cfg, batch, seq)
+    inp = graphs.bert_inputs(batch, seq)
+    g = ex.run(inp, [out])[out]
+    r = cpu.run(inp, [out])[out]
+    assert g.shape == (batch, seq, cfg.hidden)
+    np.testing.assert_allclose(g, r, atol=5e-2)
+    assert np.mean(np.abs(g - r) > 1e-3) < 0.05  # quantisation-boundary flips
+    fused = [s for s in ex.plan() if s.startswith("QuantLinear")]
+    assert len(fused) == 6 * cfg.layers
+
+
+@gpu
+def test_cuda_graph_replay_equals_eager():
+    from iconnx_b200.engine import GpuGraphExecutor
+    cfg = graphs.BertConfig(layers=1)
+    inp = graphs.bert_inputs(2, 16)
+    outs = []
+    for graphs_on in (True, False):
+        ex = GpuGraphExecutor.new()
+        out = graphs.build_bert(ex, cfg, 2, 16)
+        ex.set_cuda_graphs(graphs_on)
+        for _ in range(3):
+            outs.append(ex.run(inp, [out])[out])
+    for o in outs[1:]:
+        np.testing.assert_array_equal(o, outs[0])
