@@ -1,16 +1,20 @@
 """Benchmark of the int8 dynamic-quantization hot path on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload ffn|sweep]
-                    [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W]
+                    [--workload distilbert|bert|ffn|sweep] [--impl ours|reference]
 
 One JSON line on stdout (rank 0).  A "step" is one pass of the hot path over
 one batch of seeded synthetic input (no dataset or checkpoint exists here):
 
-* ``ffn``   (default): the int8 FFN block of the DistilBERT/BERT layer, batch
-  32 x seq 128 (M = 4096): DynamicQuantizeLinear -> MatMulInteger(768x3072)
-  -> dequant + bias -> erf-GELU -> DynamicQuantizeLinear ->
-  MatMulInteger(3072x768) -> dequant + bias.  Metric: sequences/s.
-* ``sweep``: one large-M point of the fused chain (M=65536, K=N=4096).
+* ``distilbert`` (default, config 3): the DistilBERT-base encoder, every
+  Linear int8 (DynamicQuantizeLinear -> MatMulInteger -> dequant + bias
+  [-> erf-GELU]), batch 32 x seq 128, run by the graph executor
+  (GpuGraphExecutor).  Metric: sequences/s.
+* ``bert`` (config 4): BERT-base, 12 layers, per-column weight scales and
+  zero points, batch 64 x seq 512.
+* ``ffn`` (config 2): the int8 FFN block alone, M = 4096, via the per-op API.
+* ``sweep`` (config 5): one large-M point of the fused chain (M=65536,
+  K=N=4096).  Metric: int8 TOP/s.
 
 Timing: W untimed warm-up steps, then K steps each bracketed by CUDA events
 on the launching stream, with a 256 MiB L2 flush between steps (outside the
@@ -18,8 +22,10 @@ events); barrier + synchronize on both sides; max over ranks.  Multi-GPU runs
 shard the batch: every rank processes its own batch (weak scaling, no
 collective on the data path).  ``e2e`` times the same step through the public
 API from pinned host memory, including the H2D copy of the input and the D2H
-copy of the output.  ``roofline`` is measured for the fused GEMM kernel by
-CUDA events around back-to-back launches of that kernel.
+copy of the output (encoder workloads: ``GpuGraphExecutor.run`` with host
+arrays, wall-clock).  ``roofline`` is measured for the dominant kernel (the
+GELU-fused FFN GEMM of the encoder, M x 768 x 3072) by CUDA events around
+back-to-back launches of that kernel.
 """
 
 from __future__ import annotations
@@ -142,6 +148,9 @@ class FfnWorkload:
         out, *_ = ops.dynamic_quant_linear(h, self.w2, self.ws, self.b2, x_minmax=self.mm)
         return out
 
+    def make_replay(self):
+        return _torch_graph_replay(self)
+
     def e2e_step(self):
         torch = self.torch
         x = self.x_host.to(self.device, non_blocking=True)
@@ -207,6 +216,9 @@ class SweepWorkload:
                                                 self.bias)
         return out
 
+    def make_replay(self):
+        return _torch_graph_replay(self)
+
     def e2e_step(self):
         x = self.x_host.to(self.device, non_blocking=True)
         out = self.step(x)
@@ -236,7 +248,94 @@ class SweepWorkload:
         return 2.0 * m * self.N * self.K / dt / 1e12, f"fused chain on {m} rows of the same workload"
 
 
-WORKLOADS = {"ffn": FfnWorkload, "sweep": SweepWorkload}
+def _torch_graph_replay(wl):
+    """Capture one per-op step in a CUDA graph on torch's current stream."""
+    torch = wl.torch
+    for _ in range(2):
+        wl.step()
+    torch.cuda.synchronize(wl.device)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        wl.step()
+    wl._graph = g
+    return g.replay, torch.cuda.current_stream(wl.device)
+
+
+def _ffn_gemm_probe(torch, device, M, K=768, N=3072):
+    """The GELU-fused FFN1 GEMM (dominant kernel of every encoder layer)."""
+    from iconnx_b200 import ops, synth
+    x = torch.from_numpy(synth.normal((M, K), 1.0, 0)).to(device)
+    w = ops.prepare_weight(torch.from_numpy(synth.int8_uniform((K, N), 1)).to(device))
+    b = torch.from_numpy(synth.normal((N,), 0.02, 2)).to(device)
+    ws = torch.tensor([0.01], dtype=torch.float32, device=device)
+    y, s, z = ops.gpu_dynamic_quantize_linear(x)
+    out = torch.empty((M, N), dtype=torch.float32, device=device)
+
+    def launch():
+        ops.quant_linear(y, s, z, w, ws, b, gelu=True, out=out)
+    return launch, 2.0 * M * N * K, M * K + N * K + 4 * M * N + 8 * N, \
+        f"quant_linear_gelu M={M} K={K} N={N}"
+
+
+class EncoderWorkload:
+    """Configs 3 / 4: an int8 encoder through GpuGraphExecutor."""
+
+    def __init__(self, device, kind="distilbert", seed_base=0):
+        import torch
+        from iconnx_b200 import graphs
+        from iconnx_b200.engine import GpuGraphExecutor
+        self.torch, self.device = torch, device
+        self.name = kind
+        if kind == "distilbert":
+            self.cfg, self.batch, self.seq = graphs.DISTILBERT, 32, 128
+            self.model = "DistilBERT-base (6 layers, int8 Linears, per-tensor)"
+        else:
+            self.cfg, self.batch, self.seq = graphs.BERT_BASE, 64, 512
+            self.model = "BERT-base (12 layers, int8 Linears, per-column scale + zero point)"
+        self.M = self.batch * self.seq
+        self.ex = GpuGraphExecutor.new(device.index or 0)
+        self.out = graphs.build_bert(self.ex, self.cfg, self.batch, self.seq)
+        self.inputs = graphs.bert_inputs(self.batch, self.seq, seed=6 + seed_base)
+        self.host_out = np.empty((self.batch, self.seq, self.cfg.hidden), np.float32)
+        self.ex.run(self.inputs, [self.out])        # lower + compile + warm
+        self.ex.run(self.inputs, [self.out])        # captures the CUDA graph
+        self.units_per_step = self.batch
+        self.unit = "seq/s"
+        self.launches_per_step = self.ex.kernel_launches()
+        self.gemm_ops = graphs.gemm_ops_per_sequence(self.cfg, self.seq) * self.batch
+
+    def make_replay(self):
+        stream = self.torch.cuda.ExternalStream(self.ex.stream(), device=self.device)
+        return self.ex.replay, stream
+
+    def e2e_step(self):
+        self.ex.run_device(self.inputs, [self.out])
+        self.ex.fetch(self.out, self.host_out)
+        h2d = sum(a.nbytes for a in self.inputs.values())
+        return h2d, self.host_out.nbytes
+
+    def gemm_probe(self):
+        return _ffn_gemm_probe(self.torch, self.device, self.M)
+
+    def cpu_sample(self, threads):
+        """The CPU interpreter (oracle operators) on ONE sequence, all layers."""
+        from iconnx_b200 import graphs
+        from oracle.graph_executor import CpuGraph
+        if getattr(self, "_cpu", None) is None or self._cpu[0].threads != threads:
+            cpu = CpuGraph(threads=threads)
+            self._cpu = (cpu, graphs.build_bert(cpu, self.cfg, 1, self.seq))
+        cpu, out = self._cpu
+        inp = graphs.bert_inputs(1, self.seq)
+        t0 = time.perf_counter()
+        cpu.run(inp, [out])
+        dt = time.perf_counter() - t0
+        return 1.0 / dt, (f"{self.name} encoder, 1 sequence x {self.seq} tokens, all "
+                          f"{self.cfg.layers} layers, CPU interpreter over the oracle operators")
+
+
+WORKLOADS = {"ffn": FfnWorkload, "sweep": SweepWorkload,
+             "distilbert": lambda dev, seed_base=0: EncoderWorkload(dev, "distilbert", seed_base),
+             "bert": lambda dev, seed_base=0: EncoderWorkload(dev, "bert", seed_base)}
 
 
 # ------------------------------------------------------------------ helpers
@@ -275,7 +374,16 @@ def run_reference(args):
 
     import torch
     from iconnx_b200 import synth
-    if args.workload == "ffn":
+    if args.workload in ("distilbert", "bert"):
+        from iconnx_b200 import graphs
+        w = EncoderWorkload.__new__(EncoderWorkload)
+        w.name = args.workload
+        w.cfg, w.seq = (graphs.DISTILBERT, 128) if args.workload == "distilbert" else (graphs.BERT_BASE, 512)
+        fn = lambda: EncoderWorkload.cpu_sample(w, threads)  # noqa: E731
+        unit = "seq/s"
+        cfg = {"workload": f"{args.workload} encoder (config {'3' if args.workload == 'distilbert' else '4'})",
+               "sample": "one sequence per step"}
+    elif args.workload == "ffn":
         w = FfnWorkload.__new__(FfnWorkload)
         w.batch, w.seq, w.hidden, w.ffn = 32, 128, 768, 3072
         w.x_host = torch.from_numpy(synth.normal((128, 768), 1.0, 0))
@@ -314,7 +422,7 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--workload", default="ffn", choices=sorted(WORKLOADS))
+    ap.add_argument("--workload", default="distilbert", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
@@ -336,6 +444,8 @@ def main():
     wl = WORKLOADS[args.workload](dev, seed_base=1000 * rank)
     stream = torch.cuda.current_stream(dev)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    if not hasattr(wl, "launches_per_step"):
+        wl.launches_per_step = 0
 
     def barrier():
         if pg is not None:
@@ -343,14 +453,10 @@ def main():
         torch.cuda.synchronize(dev)
 
     # ---- device-resident timing (value)
-    g = torch.cuda.CUDAGraph()
-    for _ in range(2):
-        wl.step()
-    torch.cuda.synchronize(dev)
-    with torch.cuda.graph(g):
-        wl.step()
+    replay, wstream = wl.make_replay()
+    cur = torch.cuda.current_stream(dev)
     for _ in range(args.warmup):
-        g.replay()
+        replay()
     barrier()
     clocks = ClockSampler(local)
     clocks.start()
@@ -358,20 +464,21 @@ def main():
     # sees the clocks of this workload (untimed, like the warm-up)
     t_soak = time.time()
     while time.time() - t_soak < 1.5:
-        for _ in range(20):
-            g.replay()
+        for _ in range(10):
+            replay()
         torch.cuda.synchronize(dev)
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
            for _ in range(args.steps)]
-    for s, e in evs:
-        flush.fill_(1)
-        s.record(stream)
-        g.replay()
-        e.record(stream)
+    for s_ev, e_ev in evs:
+        flush.fill_(1)                      # L2 flush, outside the events
+        wstream.wait_stream(cur)
+        s_ev.record(wstream)
+        replay()
+        e_ev.record(wstream)
+        cur.wait_stream(wstream)
     barrier()
     clk = clocks.stop()
-    step_ms = [s.elapsed_time(e) for s, e in evs]
-    total_ms = float(np.sum(step_ms))
+    total_ms = float(np.sum([s_ev.elapsed_time(e_ev) for s_ev, e_ev in evs]))
     t = torch.tensor([total_ms], device=dev)
     if pg is not None:
         pg.all_reduce(t, op=pg.ReduceOp.MAX)
@@ -382,13 +489,11 @@ def main():
     for _ in range(args.warmup):
         wl.e2e_step()
     barrier()
-    s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s_ev.record(stream)
+    t0 = time.perf_counter()
     for _ in range(args.steps):
         h2d, d2h = wl.e2e_step()
-    e_ev.record(stream)
-    barrier()
-    e2e_ms = s_ev.elapsed_time(e_ev)
+    torch.cuda.synchronize(dev)
+    e2e_ms = (time.perf_counter() - t0) * 1e3
     t = torch.tensor([e2e_ms], device=dev)
     if pg is not None:
         pg.all_reduce(t, op=pg.ReduceOp.MAX)
@@ -431,7 +536,8 @@ def main():
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "u8xs8->s32, f32 epilogue", "data": "synthetic (seeded)",
             "config": {"workload": wl.name, "M_per_gpu": wl.M,
-                       "l2": "256 MiB flush between timed steps", "parallelism": f"batch-shard x{world}"},
+                       "l2": "256 MiB flush between timed steps",
+                       "parallelism": f"batch-shard x{world} (independent executors, no collective)"},
             "e2e": {"value": e2e_value, "unit": wl.unit, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
             "gpu_launches": wl.launches_per_step * args.steps,
@@ -439,6 +545,10 @@ def main():
     if wl.name == "ffn":
         line["config"].update({"model": "DistilBERT-base FFN block (int8)", "global_batch": 32 * world,
                                "seq_len": 128})
+    if isinstance(wl, EncoderWorkload):
+        line["config"].update({"model": wl.model, "global_batch": wl.batch * world,
+                               "seq_len": wl.seq, "batch_per_gpu": wl.batch})
+        line["int8_gemm_tops_in_step"] = wl.gemm_ops / (total_ms / args.steps / 1e3) / 1e12
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         from oracle import oracle
         ncores, model = cpu_info()

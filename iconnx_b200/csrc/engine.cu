@@ -824,7 +824,9 @@ class Engine {
     // lifetimes in step units (position in order_)
     std::map<std::string, std::pair<int, int>> life;  // root -> [def, last use]
     const int end = (int)order_.size() + 1;
-    for (auto& nm : inputs_) life[nm] = {-1, -1};
+    // graph inputs keep their slot for the whole plan so replay() can
+    // re-read the inputs of the last run
+    for (auto& nm : inputs_) life[nm] = {-1, end};
     for (int pos = 0; pos < (int)order_.size(); ++pos) {
       const int idx = order_[pos];
       const NodeDef& n = nodes_[idx];

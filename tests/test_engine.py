@@ -131,3 +131,21 @@ def test_cuda_graph_replay_equals_eager():
             outs.append(ex.run(inp, [out])[out])
     for o in outs[1:]:
         np.testing.assert_array_equal(o, outs[0])
+
+
+@gpu
+def test_replay_rereads_last_inputs():
+    """replay() re-executes the plan on the inputs of the last run: graph
+    inputs must not share arena space with intermediates."""
+    from iconnx_b200.engine import GpuGraphExecutor
+    import torch
+    cfg = graphs.BertConfig(layers=2)
+    ex = GpuGraphExecutor.new()
+    out = graphs.build_bert(ex, cfg, 4, 32)
+    inp = graphs.bert_inputs(4, 32)
+    ref = ex.run(inp, [out])[out]
+    for _ in range(3):
+        ex.replay()
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(ex.fetch(out), ref)
+    np.testing.assert_array_equal(ex.run(inp, [out])[out], ref)
