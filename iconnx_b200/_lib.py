@@ -49,6 +49,7 @@ PROTOTYPES = {
     "icx_engine_set_cuda_graphs": (_i, [_vp, _i]),
     "icx_engine_kernel_launches": (_i, [_vp]),
     "icx_engine_replay": (_i, [_vp]),
+    "icx_engine_profile": (ctypes.c_char_p, [_vp]),
     "icx_engine_stream": (_vp, [_vp]),
 }
 

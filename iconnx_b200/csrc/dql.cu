@@ -133,6 +133,13 @@ __device__ __forceinline__ DqlParams dql_params(float fmn, float fmx) {
   return p;
 }
 
+// f64 division path (ties, near-ties, non-finite inputs, extreme scales);
+// kept out of line so the common path stays small.
+__device__ __noinline__ uint32_t quant_exact(float xv, double scale, float zpf) {
+  const double q = rint((double)xv / scale) + (double)zpf;
+  return q > 0.0 ? (q < 255.0 ? (uint32_t)q : 255u) : 0u;  // NaN -> 0
+}
+
 __device__ __forceinline__ uint32_t quant1(float xv, const DqlParams& p) {
   if (p.zero) return 0u;
   if (p.fast) {
@@ -144,9 +151,7 @@ __device__ __forceinline__ uint32_t quant1(float xv, const DqlParams& p) {
       return q > 0.0f ? (q < 255.0f ? (uint32_t)q : 255u) : 0u;
     }
   }
-  // f64 division path (ties, near-ties, non-finite inputs, extreme scales)
-  const double q = rint((double)xv / p.scale) + (double)p.zpf;
-  return q > 0.0 ? (q < 255.0 ? (uint32_t)q : 255u) : 0u;  // NaN -> 0
+  return quant_exact(xv, p.scale, p.zpf);
 }
 
 __device__ __forceinline__ uint32_t quant4(float4 v, const DqlParams& p,
@@ -157,7 +162,7 @@ __device__ __forceinline__ uint32_t quant4(float4 v, const DqlParams& p,
   return a | (b << 8) | (c << 16) | (d << 24);
 }
 
-__global__ void __launch_bounds__(kQuantThreads)
+__global__ void __launch_bounds__(kQuantThreads, 4)
     dql_quantize_kernel(const float* __restrict__ x, size_t n,
                         const float2* __restrict__ partials, int nparts,
                         uint8_t* __restrict__ y, float* __restrict__ scale_out,
@@ -197,11 +202,22 @@ __global__ void __launch_bounds__(kQuantThreads)
     const size_t nblk = n / 512;
     const float4* x4 = reinterpret_cast<const float4*>(x);
     uint32_t* y4 = reinterpret_cast<uint32_t*>(y);
+    // the next iteration's four loads are issued before this one is processed
+    float4 nv[4];
+    if (warp_g < nblk) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) nv[j] = __ldg(x4 + warp_g * 128 + 32 * j + lane);
+    }
     for (size_t blk = warp_g; blk < nblk; blk += nwarps) {
       const size_t base4 = blk * 128;
       float4 v[4];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) v[j] = __ldg(x4 + base4 + 32 * j + lane);
+      for (int j = 0; j < 4; ++j) v[j] = nv[j];
+      const size_t nxt = blk + nwarps;
+      if (nxt < nblk) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) nv[j] = __ldg(x4 + nxt * 128 + 32 * j + lane);
+      }
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         uint32_t sum = 0;
@@ -276,7 +292,7 @@ extern "C" int icx_dql_f32_u8(void* stream, const float* d_x, size_t n,
   size_t work = vec16 ? n / 16 : n;
   size_t qb = (work + kQuantThreads - 1) / kQuantThreads;
   if (qb < 1) qb = 1;
-  if (qb > 148 * 8) qb = 148 * 8;
+  if (qb > 148 * 4) qb = 148 * 4;
   dql_quantize_kernel<<<(int)qb, kQuantThreads, 0, s>>>(
       d_x, n, static_cast<const float2*>(d_workspace), blocks, d_y, d_scale,
       d_zp, d_rowsum, row_len ? row_len : 1, vec16);
@@ -303,7 +319,7 @@ extern "C" int icx_dql_quantize_f32_u8(void* stream, const float* d_x, size_t n,
   size_t work = vec16 ? n / 16 : n;
   size_t qb = (work + kQuantThreads - 1) / kQuantThreads;
   if (qb < 1) qb = 1;
-  if (qb > 148 * 8) qb = 148 * 8;
+  if (qb > 148 * 4) qb = 148 * 4;
   dql_quantize_kernel<<<(int)qb, kQuantThreads, 0, s>>>(
       d_x, n, reinterpret_cast<const float2*>(d_minmax), n_minmax, d_y, d_scale, d_zp,
       d_rowsum, row_len ? row_len : 1, vec16);
@@ -382,7 +398,7 @@ extern "C" int icx_dql_f32_u8_noalloc(void* stream, const float* d_x, size_t n,
   size_t work = vec16 ? n / 16 : n;
   size_t qb = (work + kQuantThreads - 1) / kQuantThreads;
   if (qb < 1) qb = 1;
-  if (qb > 148 * 8) qb = 148 * 8;
+  if (qb > 148 * 4) qb = 148 * 4;
   dql_quantize_kernel<<<(int)qb, kQuantThreads, 0, s>>>(
       d_x, n, scratch, blocks, d_y, d_scale, d_zp, d_rowsum, row_len ? row_len : 1, vec16);
   ICX_LAUNCH_CHECK();

@@ -142,6 +142,15 @@ struct FusedQL {
   bool gelu = false;
 };
 
+// One fused attention block: Reshape/Transpose of Q, K, V -> MatMul ->
+// Div(c) -> Add(mask) -> Softmax -> MatMul -> Transpose -> Reshape.
+struct FusedAttn {
+  std::string q, k, v, mask, scores, out;
+  float c = 1.0f;
+  int64_t B = 0, S = 0, H = 0, nh = 0, dh = 0;
+  bool mask_per_batch = true;
+};
+
 struct Step {
   std::string node, op, out;
   std::function<int(cudaStream_t)> fn;
@@ -293,6 +302,62 @@ class Engine {
     return s;
   }
 
+  // Runs the compiled plan once more (eagerly, on the inputs of the last run)
+  // with a CUDA event pair around every step and returns one line per step:
+  // "<gpu_ms>\t<op>\t<node>\t<output>".  The counterpart of the reference's
+  // run_with_profiling / GpuEventTimer (src/cuda/executor/variants.rs:415,
+  // src/cuda/inference/gpu_event_timer.rs:1-45).
+  int profile(std::string* text) {
+    ICX_REQUIRE(compiled_, "profile: no compiled plan (call run first)");
+    ICX_CUDA(cudaSetDevice(device_));
+    // Every step is captured alone, kReps times in a row, into a CUDA graph
+    // and timed with an event pair around its replay: device time only,
+    // without the host launch gaps an eager per-step measurement includes.
+    // Steps are idempotent, so repeating one leaves the state unchanged.
+    constexpr int kReps = 10;
+    cudaEvent_t e0, e1;
+    ICX_CUDA(cudaEventCreate(&e0));
+    ICX_CUDA(cudaEventCreate(&e1));
+    text->clear();
+    int rc = ICX_OK;
+    for (size_t i = 0; i < steps_.size() && !rc; ++i) {
+      cudaGraph_t g = nullptr;
+      cudaGraphExec_t ge = nullptr;
+      ICX_CUDA(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
+      for (int r = 0; r < kReps && !rc; ++r) rc = steps_[i].fn(stream_);
+      cudaError_t ce = cudaStreamEndCapture(stream_, &g);
+      if (rc || ce != cudaSuccess) {
+        if (g) cudaGraphDestroy(g);
+        if (!rc) {
+          set_error("profile capture failed: %s", cudaGetErrorString(ce));
+          rc = ICX_ERR_CUDA;
+        }
+        break;
+      }
+      ce = cudaGraphInstantiate(&ge, g, 0);
+      cudaGraphDestroy(g);
+      if (ce != cudaSuccess) {
+        set_error("profile instantiate failed: %s", cudaGetErrorString(ce));
+        rc = ICX_ERR_CUDA;
+        break;
+      }
+      cudaGraphLaunch(ge, stream_);  // warm
+      cudaEventRecord(e0, stream_);
+      cudaGraphLaunch(ge, stream_);
+      cudaEventRecord(e1, stream_);
+      cudaStreamSynchronize(stream_);
+      float ms = 0;
+      cudaEventElapsedTime(&ms, e0, e1);
+      cudaGraphExecDestroy(ge);
+      char buf[64];
+      snprintf(buf, sizeof(buf), "%.4f\t", ms / kReps);
+      *text += buf + steps_[i].op + "\t" + steps_[i].node + "\t" + steps_[i].out + "\n";
+    }
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    return rc;
+  }
+
   // Re-executes the compiled plan on the device-resident inputs of the last
   // run, asynchronously on the engine's stream (no copies, no sync).
   int replay() {
@@ -369,6 +434,7 @@ class Engine {
     vals_.clear();
     steps_.clear();
     fused_.clear();
+    attn_.clear();
     skip_.clear();
     dql_mode_.clear();
     minmax_count_.clear();
@@ -742,6 +808,7 @@ class Engine {
       fused_[idx] = f;
       skip_.erase(idx);  // the MatMulInteger position runs the fused kernel
     }
+    fuse_attention();
     // intermediates of fused chains are never materialised
     for (int idx : order_) {
       if (!skip_.count(idx)) continue;
@@ -750,6 +817,12 @@ class Engine {
     for (auto& kv : fused_) {
       for (auto& o : nodes_[kv.first].out) vals_[o].needed = false;
       vals_[kv.second.out].needed = true;
+    }
+    for (auto& kv : attn_) {
+      vals_[kv.second.scores].needed = true;  // scratch for scores / probabilities
+      Val& o = vals_[kv.second.out];
+      o.needed = true;
+      o.alias.clear();
     }
     // producer-fused min/max for DynamicQuantizeLinear
     int slot = 0;
@@ -771,6 +844,91 @@ class Engine {
       ++slot;
     }
     n_slots_ = slot;
+  }
+
+  // Reshape(t, [0, 0, nh, dh]) -> Transpose(perm) feeding `use`: returns t.
+  bool head_split(const std::string& v, const std::vector<int64_t>& perm, std::string* src,
+                  std::vector<int>* chain) {
+    const int tr = producer_op(v, "Transpose");
+    if (tr < 0 || sole_consumer(v) < 0 || is_requested(v)) return false;
+    const auto* p = nodes_[tr].getints("perm");
+    if (!p || *p != perm) return false;
+    const int rs = producer_op(nodes_[tr].in[0], "Reshape");
+    if (rs < 0 || sole_consumer(nodes_[tr].in[0]) != tr || is_requested(nodes_[tr].in[0])) return false;
+    const Val& x = vals_[nodes_[rs].in[0]];
+    const Val& r = vals_[nodes_[rs].out[0]];
+    if (x.dtype != ICX_F32 || x.shape.size() != 3 || r.shape.size() != 4) return false;
+    if (r.shape[0] != x.shape[0] || r.shape[1] != x.shape[1] || r.shape[2] * r.shape[3] != x.shape[2])
+      return false;
+    *src = nodes_[rs].in[0];
+    chain->push_back(rs);
+    chain->push_back(tr);
+    return true;
+  }
+
+  void fuse_attention() {
+    for (int idx : order_) {
+      const NodeDef& sm = nodes_[idx];
+      if (sm.op != "Softmax" || skip_.count(idx)) continue;
+      std::vector<int> chain{idx};
+      FusedAttn a;
+      std::string x = sm.in[0];
+      const int add = producer_op(x, "Add");
+      std::string divout = x;
+      if (add >= 0) {
+        if (sole_consumer(x) != idx || is_requested(x)) continue;
+        const NodeDef& an = nodes_[add];
+        const int d0 = producer_op(an.in[0], "Div"), d1 = producer_op(an.in[1], "Div");
+        const int which = d0 >= 0 ? 0 : (d1 >= 0 ? 1 : -1);
+        if (which < 0) continue;
+        divout = an.in[which];
+        a.mask = an.in[1 - which];
+        chain.push_back(add);
+      }
+      const int dv = producer_op(divout, "Div");
+      if (dv < 0 || sole_consumer(divout) != (add >= 0 ? add : idx) || is_requested(divout)) continue;
+      if (!scalar_f32(init_of(nodes_[dv].in[1]), &a.c)) continue;
+      chain.push_back(dv);
+      a.scores = nodes_[dv].in[0];
+      const int mm1 = producer_op(a.scores, "MatMul");
+      if (mm1 < 0 || sole_consumer(a.scores) != dv || is_requested(a.scores)) continue;
+      chain.push_back(mm1);
+      if (!head_split(nodes_[mm1].in[0], {0, 2, 1, 3}, &a.q, &chain)) continue;
+      if (!head_split(nodes_[mm1].in[1], {0, 2, 3, 1}, &a.k, &chain)) continue;
+      const int mm2 = sole_consumer(sm.out[0]);
+      if (mm2 < 0 || nodes_[mm2].op != "MatMul" || nodes_[mm2].in[0] != sm.out[0] || is_requested(sm.out[0]))
+        continue;
+      chain.push_back(mm2);
+      if (!head_split(nodes_[mm2].in[1], {0, 2, 1, 3}, &a.v, &chain)) continue;
+      const int tr = sole_consumer(nodes_[mm2].out[0]);
+      if (tr < 0 || nodes_[tr].op != "Transpose" || is_requested(nodes_[mm2].out[0])) continue;
+      const auto* perm = nodes_[tr].getints("perm");
+      if (!perm || *perm != std::vector<int64_t>{0, 2, 1, 3}) continue;
+      chain.push_back(tr);
+      const int rs = sole_consumer(nodes_[tr].out[0]);
+      if (rs < 0 || nodes_[rs].op != "Reshape" || is_requested(nodes_[tr].out[0])) continue;
+      const Val& qv = vals_[a.q];
+      const Val& sv = vals_[a.scores];
+      const Val& ov = vals_[nodes_[rs].out[0]];
+      a.B = qv.shape[0];
+      a.S = qv.shape[1];
+      a.H = qv.shape[2];
+      a.nh = sv.shape[1];
+      a.dh = a.H / a.nh;
+      if (vals_[a.k].shape != qv.shape || vals_[a.v].shape != qv.shape || ov.shape != qv.shape ||
+          sv.shape != Shape({a.B, a.nh, a.S, a.S}))
+        continue;
+      if (!a.mask.empty()) {
+        const Shape& ms = vals_[a.mask].shape;
+        const bool pb = ms == Shape({a.B, 1, 1, a.S});
+        const bool shared = ms == Shape({1, 1, 1, a.S}) || ms == Shape({a.S});
+        if (!pb && !shared) continue;
+        a.mask_per_batch = pb;
+      }
+      a.out = nodes_[rs].out[0];
+      for (int c : chain) skip_.insert(c);
+      attn_[rs] = a;
+    }
   }
 
   // ---------------------------------------------------- weights upload
@@ -837,6 +995,17 @@ class Engine {
         const FusedQL& f = fit->second;
         if (!life.count(f.out)) life[f.out] = {pos, pos};
         for (const std::string* i : {&f.q, &f.s, &f.z}) {
+          const std::string r = root(*i);
+          auto it = life.find(r);
+          if (it != life.end()) it->second.second = std::max(it->second.second, pos);
+        }
+      }
+      auto ait = attn_.find(idx);
+      if (ait != attn_.end()) {
+        const FusedAttn& at = ait->second;
+        if (!life.count(at.scores)) life[at.scores] = {pos, pos};
+        for (const std::string* i : {&at.q, &at.k, &at.v, &at.mask}) {
+          if (i->empty()) continue;
           const std::string r = root(*i);
           auto it = life.find(r);
           if (it != life.end()) it->second.second = std::max(it->second.second, pos);
@@ -917,7 +1086,10 @@ class Engine {
       if (skip_.count(idx)) continue;
       const NodeDef& n = nodes_[idx];
       auto fit = fused_.find(idx);
-      int rc = fit != fused_.end() ? step_fused(idx, fit->second) : step_node(idx);
+      auto ait = attn_.find(idx);
+      int rc = fit != fused_.end()   ? step_fused(idx, fit->second)
+               : ait != attn_.end() ? step_attention(idx, ait->second)
+                                    : step_node(idx);
       if (rc) return rc;
     }
     return ICX_OK;
@@ -958,6 +1130,74 @@ class Engine {
                               (size_t)M, (size_t)K, (size_t)pw.N, wsp, ws_pc, bzp, bz_pc, bp,
                               gelu ? 1 : 0, out, mm, mmc);
     }, 1);
+    return ICX_OK;
+  }
+
+  // Attention without any transpose: two pointer-array batched SGEMMs read
+  // Q, K, V in place from [B, S, H] (head h is the column block h*dh) and
+  // write the context straight back into [B, S, H]; between them one kernel
+  // applies Div(c), Add(mask) and Softmax with the rounding of those ops.
+  int step_attention(int idx, const FusedAttn& a) {
+    const NodeDef& n = nodes_[idx];
+    const int64_t nb = a.B * a.nh;
+    std::vector<const float*> hA1(nb), hB1(nb), hA2(nb), hB2(nb);
+    std::vector<float*> hC1(nb), hC2(nb);
+    const float* q = static_cast<const float*>(resolve(a.q));
+    const float* k = static_cast<const float*>(resolve(a.k));
+    const float* v = static_cast<const float*>(resolve(a.v));
+    float* sc = static_cast<float*>(resolve(a.scores));
+    float* out = static_cast<float*>(resolve(a.out));
+    for (int64_t b = 0; b < a.B; ++b)
+      for (int64_t h = 0; h < a.nh; ++h) {
+        const int64_t i = b * a.nh + h;
+        const int64_t off = b * a.S * a.H + h * a.dh;
+        hA1[i] = k + off;
+        hB1[i] = q + off;
+        hC1[i] = sc + i * a.S * a.S;
+        hA2[i] = v + off;
+        hB2[i] = sc + i * a.S * a.S;
+        hC2[i] = out + off;
+      }
+    void* dptr = nullptr;
+    ICX_CUDA(cudaMalloc(&dptr, (size_t)nb * 6 * sizeof(void*)));
+    scratch_.push_back(dptr);
+    void** d = static_cast<void**>(dptr);
+    const size_t pb = (size_t)nb * sizeof(void*);
+    ICX_CUDA(cudaMemcpy(d + 0 * nb, hA1.data(), pb, cudaMemcpyHostToDevice));
+    ICX_CUDA(cudaMemcpy(d + 1 * nb, hB1.data(), pb, cudaMemcpyHostToDevice));
+    ICX_CUDA(cudaMemcpy(d + 2 * nb, hC1.data(), pb, cudaMemcpyHostToDevice));
+    ICX_CUDA(cudaMemcpy(d + 3 * nb, hA2.data(), pb, cudaMemcpyHostToDevice));
+    ICX_CUDA(cudaMemcpy(d + 4 * nb, hB2.data(), pb, cudaMemcpyHostToDevice));
+    ICX_CUDA(cudaMemcpy(d + 5 * nb, hC2.data(), pb, cudaMemcpyHostToDevice));
+    const float* mask = a.mask.empty() ? nullptr : static_cast<const float*>(resolve(a.mask));
+    const FusedAttn at = a;
+    cublasHandle_t hdl = blas_;
+    add_step(n, "Attention", a.out, [=](cudaStream_t s) {
+      const float one = 1.0f, zero = 0.0f;
+      // scores[b,h] (row-major S x S) = Q_bh K_bh^T
+      cublasStatus_t st = cublasSgemmBatched(
+          hdl, CUBLAS_OP_T, CUBLAS_OP_N, (int)at.S, (int)at.S, (int)at.dh, &one,
+          reinterpret_cast<const float* const*>(d + 0 * nb), (int)at.H,
+          reinterpret_cast<const float* const*>(d + 1 * nb), (int)at.H, &zero,
+          reinterpret_cast<float* const*>(d + 2 * nb), (int)at.S, (int)nb);
+      if (st != CUBLAS_STATUS_SUCCESS) {
+        set_error("cublasSgemmBatched (scores) failed (%d)", (int)st);
+        return ICX_ERR_CUDA;
+      }
+      int rc = launch_scale_mask_softmax(s, sc, sc, (size_t)(nb * at.S), (size_t)at.S, at.c, mask,
+                                         at.mask_per_batch ? (size_t)(at.nh * at.S) : 0);
+      if (rc) return rc;
+      // ctx[b, :, h*dh:(h+1)*dh] = P_bh V_bh
+      st = cublasSgemmBatched(hdl, CUBLAS_OP_N, CUBLAS_OP_N, (int)at.dh, (int)at.S, (int)at.S, &one,
+                              reinterpret_cast<const float* const*>(d + 3 * nb), (int)at.H,
+                              reinterpret_cast<const float* const*>(d + 4 * nb), (int)at.S, &zero,
+                              reinterpret_cast<float* const*>(d + 5 * nb), (int)at.H, (int)nb);
+      if (st != CUBLAS_STATUS_SUCCESS) {
+        set_error("cublasSgemmBatched (context) failed (%d)", (int)st);
+        return ICX_ERR_CUDA;
+      }
+      return ICX_OK;
+    }, 3);
     return ICX_OK;
   }
 
@@ -1214,6 +1454,7 @@ class Engine {
   std::vector<int> order_;
   std::unordered_map<std::string, Val> vals_;
   std::map<int, FusedQL> fused_;
+  std::map<int, FusedAttn> attn_;
   std::set<int> skip_;
   std::map<int, int> dql_mode_;
   int n_slots_ = 0;
@@ -1344,3 +1585,9 @@ extern "C" int icx_engine_replay(icx_engine* h) {
 }
 
 extern "C" void* icx_engine_stream(icx_engine* h) { return h ? (void*)h->e->stream() : nullptr; }
+
+extern "C" const char* icx_engine_profile(icx_engine* h) {
+  if (!h) return nullptr;
+  if (h->e->profile(&h->plan) != ICX_OK) return nullptr;
+  return h->plan.c_str();
+}

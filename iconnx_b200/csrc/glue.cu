@@ -103,6 +103,35 @@ __global__ void binary_rowvec_kernel(const float4* __restrict__ a, const float4*
   }
 }
 
+// one operand is a single element
+template <int OP>
+__global__ void binary_scalar_kernel(const float* __restrict__ a, const float* __restrict__ b,
+                                     float* __restrict__ o, size_t n, int scalar_is_a) {
+  const float sv = scalar_is_a ? a[0] : b[0];
+  const float* v = scalar_is_a ? b : a;
+  const size_t stride = (size_t)gridDim.x * blockDim.x;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
+    o[i] = scalar_is_a ? bin<OP>(sv, v[i]) : bin<OP>(v[i], sv);
+}
+
+// general broadcast with 32-bit index arithmetic (n < 2^31)
+template <int OP>
+__global__ void binary_bcast32_kernel(const float* __restrict__ a, const float* __restrict__ b,
+                                      float* __restrict__ o, unsigned n, BcastShape sh) {
+  const unsigned stride = gridDim.x * blockDim.x;
+  for (unsigned i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    unsigned rem = i, ia = 0, ib = 0;
+    for (int d = sh.rank - 1; d >= 0; --d) {
+      const unsigned ext = (unsigned)sh.out[d];
+      const unsigned c = rem % ext;
+      rem /= ext;
+      ia += c * (unsigned)sh.sa[d];
+      ib += c * (unsigned)sh.sb[d];
+    }
+    o[i] = bin<OP>(a[ia], b[ib]);
+  }
+}
+
 template <int OP>
 __global__ void binary_bcast_kernel(const float* __restrict__ a, const float* __restrict__ b,
                                     float* __restrict__ o, size_t n, BcastShape sh) {
@@ -173,6 +202,19 @@ int launch_binary(cudaStream_t s, int op, const float* a, const std::vector<int6
       return ICX_OK;
     }
   }
+  if (numel(ashape) == 1 || numel(bshape) == 1) {
+    const int sa = numel(ashape) == 1 && numel(bshape) != 1;
+#define ICX_SC(OPC) binary_scalar_kernel<OPC><<<elt_blocks(n), kEltThreads, 0, s>>>(a, b, out, n, sa)
+    switch (op) {
+      case kAdd: ICX_SC(kAdd); break;
+      case kSub: ICX_SC(kSub); break;
+      case kMul: ICX_SC(kMul); break;
+      default: ICX_SC(kDiv); break;
+    }
+#undef ICX_SC
+    ICX_LAUNCH_CHECK();
+    return ICX_OK;
+  }
   BcastShape sh{};
   sh.rank = (int)oshape.size();
   ICX_REQUIRE(sh.rank <= kMaxRank, "broadcast: rank %d > %d", sh.rank, kMaxRank);
@@ -192,7 +234,11 @@ int launch_binary(cudaStream_t s, int op, const float* a, const std::vector<int6
   for (int d = 0; d < sh.rank; ++d) sh.out[d] = oshape[d];
   strides(ashape, sh.sa);
   strides(bshape, sh.sb);
-#define ICX_BC(OPC) binary_bcast_kernel<OPC><<<elt_blocks(n), kEltThreads, 0, s>>>(a, b, out, n, sh)
+#define ICX_BC(OPC)                                                                         \
+  if (n < (1u << 31))                                                                       \
+    binary_bcast32_kernel<OPC><<<elt_blocks(n), kEltThreads, 0, s>>>(a, b, out, (unsigned)n, sh); \
+  else                                                                                      \
+    binary_bcast_kernel<OPC><<<elt_blocks(n), kEltThreads, 0, s>>>(a, b, out, n, sh)
   switch (op) {
     case kAdd: ICX_BC(kAdd); break;
     case kSub: ICX_BC(kSub); break;
@@ -283,8 +329,10 @@ __global__ void __launch_bounds__(32 * kLnWarps)
 }
 
 int layernorm_partials(size_t rows) {
+  // grid-stride over rows with at most 2 blocks per SM: few partials for
+  // the DynamicQuantizeLinear that reads them
   size_t b = (rows + kLnWarps - 1) / kLnWarps;
-  if (b > (size_t)ICX_MAX_MINMAX_PARTIALS) b = ICX_MAX_MINMAX_PARTIALS;
+  if (b > 148 * 2) b = 148 * 2;
   return b < 1 ? 1 : (int)b;
 }
 
@@ -341,6 +389,70 @@ __global__ void softmax_kernel(const float* __restrict__ x, float* __restrict__ 
   }
 }
 
+// Attention-score softmax fused with its two producers: y = softmax(x / c +
+// mask[b, :]) over the last axis, with the division and the addition each
+// rounded exactly as the separate Div and Add ops round them.  Rows are
+// [batch, heads, queries]; the additive mask has one row of D per batch
+// (broadcast over heads and queries), or is absent.  In place is allowed.
+template <int PER_LANE>
+__global__ void scale_mask_softmax_kernel(const float* __restrict__ x, float* __restrict__ y,
+                                          int rows, int D, float c,
+                                          const float* __restrict__ mask, int rows_per_batch) {
+  const int lane = threadIdx.x & 31;
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const float* xr = x + (size_t)row * D;
+  float* yr = y + (size_t)row * D;
+  const float* mr = mask ? mask + (size_t)(row / rows_per_batch) * D : nullptr;
+  float v[PER_LANE];
+  float m = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < PER_LANE; ++j) {
+    const int col = lane + 32 * j;
+    float t = -INFINITY;
+    if (col < D) {
+      t = __fdiv_rn(xr[col], c);
+      if (mr) t = __fadd_rn(t, mr[col]);
+    }
+    v[j] = t;
+    m = fmaxf(m, t);
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  float sum = 0.0f;
+#pragma unroll
+  for (int j = 0; j < PER_LANE; ++j) {
+    const int col = lane + 32 * j;
+    v[j] = col < D ? expf(v[j] - m) : 0.0f;
+    sum += v[j];
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  const float inv = 1.0f / sum;
+#pragma unroll
+  for (int j = 0; j < PER_LANE; ++j) {
+    const int col = lane + 32 * j;
+    if (col < D) yr[col] = v[j] * inv;
+  }
+}
+
+int launch_scale_mask_softmax(cudaStream_t s, const float* x, float* y, size_t rows, size_t D,
+                              float c, const float* mask, size_t rows_per_batch) {
+  ICX_REQUIRE(D >= 1 && D <= 1024, "Softmax: last dimension %zu unsupported (1..1024)", D);
+  if (rows == 0) return ICX_OK;
+  const int wpb = 8;
+  const unsigned grid = (unsigned)((rows + wpb - 1) / wpb);
+  const int rpb = (int)(rows_per_batch ? rows_per_batch : rows);
+  if (D <= 128)
+    scale_mask_softmax_kernel<4><<<grid, 32 * wpb, 0, s>>>(x, y, (int)rows, (int)D, c, mask, rpb);
+  else if (D <= 512)
+    scale_mask_softmax_kernel<16><<<grid, 32 * wpb, 0, s>>>(x, y, (int)rows, (int)D, c, mask, rpb);
+  else
+    scale_mask_softmax_kernel<32><<<grid, 32 * wpb, 0, s>>>(x, y, (int)rows, (int)D, c, mask, rpb);
+  ICX_LAUNCH_CHECK();
+  return ICX_OK;
+}
+
 int launch_softmax(cudaStream_t s, const float* x, float* y, size_t rows, size_t D) {
   ICX_REQUIRE(D >= 1 && D <= 1024, "Softmax: last dimension %zu unsupported (1..1024)", D);
   if (rows == 0) return ICX_OK;
@@ -356,6 +468,22 @@ struct PermShape {
   int64_t out[kMaxRank];
   int64_t in_stride[kMaxRank];  // input element stride of each output axis
 };
+
+template <typename T>
+__global__ void transpose32_kernel(const T* __restrict__ x, T* __restrict__ y, unsigned n,
+                                   PermShape ps) {
+  const unsigned stride = gridDim.x * blockDim.x;
+  for (unsigned i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    unsigned rem = i, src = 0;
+    for (int d = ps.rank - 1; d >= 0; --d) {
+      const unsigned ext = (unsigned)ps.out[d];
+      const unsigned c = rem % ext;
+      rem /= ext;
+      src += c * (unsigned)ps.in_stride[d];
+    }
+    y[i] = x[src];
+  }
+}
 
 template <typename T>
 __global__ void transpose_kernel(const T* __restrict__ x, T* __restrict__ y, size_t n,
@@ -398,8 +526,12 @@ int launch_transpose(cudaStream_t s, const void* x, int elem_bytes,
           static_cast<const uint8_t*>(x), static_cast<uint8_t*>(y), n, ps);
       break;
     case 4:
-      transpose_kernel<uint32_t><<<elt_blocks(n), kEltThreads, 0, s>>>(
-          static_cast<const uint32_t*>(x), static_cast<uint32_t*>(y), n, ps);
+      if (n < (1u << 31))
+        transpose32_kernel<uint32_t><<<elt_blocks(n), kEltThreads, 0, s>>>(
+            static_cast<const uint32_t*>(x), static_cast<uint32_t*>(y), (unsigned)n, ps);
+      else
+        transpose_kernel<uint32_t><<<elt_blocks(n), kEltThreads, 0, s>>>(
+            static_cast<const uint32_t*>(x), static_cast<uint32_t*>(y), n, ps);
       break;
     case 8:
       transpose_kernel<uint64_t><<<elt_blocks(n), kEltThreads, 0, s>>>(

@@ -23,6 +23,8 @@ int launch_binary(cudaStream_t s, int op, const float* a, const std::vector<int6
 int layernorm_partials(size_t rows);
 int launch_layernorm(cudaStream_t s, const float* x, const float* gamma, const float* beta,
                      float* y, size_t rows, size_t D, float eps, float* minmax, int* n_minmax);
+int launch_scale_mask_softmax(cudaStream_t s, const float* x, float* y, size_t rows, size_t D,
+                              float c, const float* mask, size_t rows_per_batch);
 int launch_softmax(cudaStream_t s, const float* x, float* y, size_t rows, size_t D);
 int launch_transpose(cudaStream_t s, const void* x, int elem_bytes,
                      const std::vector<int64_t>& in_shape, const std::vector<int64_t>& perm,

@@ -163,6 +163,31 @@ class GpuGraphExecutor:
         """The compiled launch plan, one 'op node -> output' line per step."""
         return [ln for ln in self._L.icx_engine_plan(self._h).decode().splitlines() if ln]
 
+    def run_with_profiling(self, inputs: dict, outputs) -> tuple[dict, list]:
+        """Runs, then times every step of the plan with CUDA events (like the
+        reference's run_with_profiling).  Returns (outputs, [(ms, op, node, out)])."""
+        res = self.run(inputs, outputs)
+        txt = self._L.icx_engine_profile(self._h)
+        if txt is None:
+            raise IcxError(-2, self._L.icx_last_error().decode())
+        prof = []
+        for ln in txt.decode().splitlines():
+            ms, op, node, out = ln.split("\t")
+            prof.append((float(ms), op, node, out))
+        return res, prof
+
+    @staticmethod
+    def profile_summary(prof) -> str:
+        """Per-op-type totals, like ProfileData::print_summary."""
+        agg = {}
+        for ms, op, _, _ in prof:
+            t, c = agg.get(op, (0.0, 0))
+            agg[op] = (t + ms, c + 1)
+        total = sum(t for t, _ in agg.values()) or 1.0
+        lines = [f"{t * 1e3:10.1f} us {100 * t / total:5.1f}% {c:4d}  {op}"
+                 for op, (t, c) in sorted(agg.items(), key=lambda kv: -kv[1][0])]
+        return "\n".join(lines + [f"total {total * 1e3:.1f} us"])
+
     def replay(self) -> None:
         """Re-run the compiled plan on the device-resident inputs of the last
         run (asynchronous, on :meth:`stream`)."""

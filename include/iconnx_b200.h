@@ -260,6 +260,11 @@ ICX_API int icx_engine_set_cuda_graphs(icx_engine* e, int enabled);
  * last run: enqueued on the engine's stream, no copies, no synchronisation
  * (device-resident throughput measurement). */
 ICX_API int icx_engine_replay(icx_engine* e);
+/* Per-step GPU times of one more eager execution of the compiled plan on the
+ * last run's inputs: lines "<ms>\t<op>\t<node>\t<output>" (NULL on error).
+ * Replaces run_with_profiling (src/cuda/executor/variants.rs:415) and its
+ * ProfileData (src/cuda/inference/mod.rs:88-164). */
+ICX_API const char* icx_engine_profile(icx_engine* e);
 /* The engine's CUDA stream (cudaStream_t as void*). */
 ICX_API void* icx_engine_stream(icx_engine* e);
 /* Kernel launches per run of the compiled plan. */

@@ -113,8 +113,11 @@ def test_encoder_matches_cpu_interpreter(cfg, batch, seq):
     assert g.shape == (batch, seq, cfg.hidden)
     np.testing.assert_allclose(g, r, atol=5e-2)
     assert np.mean(np.abs(g - r) > 1e-3) < 0.05  # quantisation-boundary flips
-    fused = [s for s in ex.plan() if s.startswith("QuantLinear")]
+    plan = ex.plan()
+    fused = [s for s in plan if s.startswith("QuantLinear")]
     assert len(fused) == 6 * cfg.layers
+    assert len([s for s in plan if s.startswith("Attention ")]) == cfg.layers
+    assert not any(s.startswith(("Transpose", "Softmax", "MatMul ")) for s in plan)
 
 
 @gpu
