@@ -120,6 +120,10 @@ struct Prepared {  // int8 weight in the tensor-core operand layout
   void* bt = nullptr;
   int32_t* colsum = nullptr;
   int64_t K = 0, N = 0;
+  // merged weights only: per-column scale, bias and zero point of the parts
+  float* ws = nullptr;
+  float* bias = nullptr;
+  int8_t* bz = nullptr;
 };
 
 struct Val {
@@ -138,14 +142,16 @@ struct Val {
 
 // One fused QuantLinear (step 3 above).
 struct FusedQL {
-  std::string q, s, z, w, ws, bz, bias, out;
+  std::string q, s, z, w, ws, bz, bias, residual, out;
   bool gelu = false;
+  std::vector<FusedQL> parts;  // non-empty: several Linears merged along N
 };
 
 // One fused attention block: Reshape/Transpose of Q, K, V -> MatMul ->
 // Div(c) -> Add(mask) -> Softmax -> MatMul -> Transpose -> Reshape.
 struct FusedAttn {
   std::string q, k, v, mask, scores, out;
+  int64_t ld = 0, off_q = 0, off_k = 0, off_v = 0;  // row stride / column offsets of q, k, v
   float c = 1.0f;
   int64_t B = 0, S = 0, H = 0, nh = 0, dh = 0;
   bool mask_per_batch = true;
@@ -390,6 +396,9 @@ class Engine {
     for (auto& kv : prepared_) {
       cudaFree(kv.second.bt);
       cudaFree(kv.second.colsum);
+      if (kv.second.ws) cudaFree(kv.second.ws);
+      if (kv.second.bias) cudaFree(kv.second.bias);
+      if (kv.second.bz) cudaFree(kv.second.bz);
     }
     for (auto& kv : inits_)
       if (kv.second->dev) cudaFree(kv.second->dev);
@@ -716,6 +725,12 @@ class Engine {
     return std::find(pending_outputs_.begin(), pending_outputs_.end(), v) != pending_outputs_.end();
   }
 
+  int pos_of(int node) const {
+    for (size_t i = 0; i < order_.size(); ++i)
+      if (order_[i] == node) return (int)i;
+    return -1;
+  }
+
   void fuse() {
     for (int idx : order_) {
       const NodeDef& mm = nodes_[idx];
@@ -801,6 +816,21 @@ class Engine {
           }
         }
       }
+      // [residual Add(out, r)] with r ready before this kernel runs
+      if (!f.gelu && sole_consumer(cur) >= 0 && !is_requested(cur)) {
+        const int ra = sole_consumer(cur);
+        const std::string* r = nodes_[ra].op == "Add" ? other(nodes_[ra], cur) : nullptr;
+        if (r && *r != cur) {
+          const Val& rv = vals_[*r];
+          const int rp = rv.producer;
+          const bool ready = rv.is_input || rv.init || (rp >= 0 && pos_of(rp) < pos_of(idx));
+          if (ready && rv.dtype == ICX_F32 && rv.shape == vals_[cur].shape) {
+            f.residual = *r;
+            chain.push_back(ra);
+            cur = nodes_[ra].out[0];
+          }
+        }
+      }
       f.out = cur;
       for (int c : chain) skip_.insert(c);
       // the scale product is computed inside the kernel when nothing else reads it
@@ -809,6 +839,7 @@ class Engine {
       skip_.erase(idx);  // the MatMulInteger position runs the fused kernel
     }
     fuse_attention();
+    merge_qkv();
     // intermediates of fused chains are never materialised
     for (int idx : order_) {
       if (!skip_.count(idx)) continue;
@@ -818,8 +849,12 @@ class Engine {
       for (auto& o : nodes_[kv.first].out) vals_[o].needed = false;
       vals_[kv.second.out].needed = true;
     }
+    for (auto& kv : fused_)
+      for (auto& part : kv.second.parts) vals_[part.out].needed = false;
     for (auto& kv : attn_) {
-      vals_[kv.second.scores].needed = true;  // scratch for scores / probabilities
+      const FusedAttn& a = kv.second;
+      // scratch for scores / probabilities (cuBLAS path only)
+      vals_[a.scores].needed = !attention_supported(a.dh, a.ld ? a.ld : a.H, a.H);
       Val& o = vals_[kv.second.out];
       o.needed = true;
       o.alias.clear();
@@ -931,6 +966,60 @@ class Engine {
     }
   }
 
+  // Q, K and V projections of one attention block read the same quantised
+  // input: run them as ONE GEMM over the concatenated weights [K, 3N]; the
+  // attention then reads q / k / v in place with a row stride of 3N.
+  void merge_qkv() {
+    for (auto& akv : attn_) {
+      FusedAttn& a = akv.second;
+      int ids[3] = {-1, -1, -1};
+      const std::string* outs[3] = {&a.q, &a.k, &a.v};
+      for (auto& kv : fused_)
+        for (int t = 0; t < 3; ++t)
+          if (kv.second.out == *outs[t]) ids[t] = kv.first;
+      if (ids[0] < 0 || ids[1] < 0 || ids[2] < 0) continue;
+      const FusedQL& f0 = fused_[ids[0]];
+      bool ok = true;
+      for (int t = 0; t < 3; ++t) {
+        const FusedQL& f = fused_[ids[t]];
+        if (f.q != f0.q || f.s != f0.s || f.z != f0.z || f.gelu || !f.residual.empty() ||
+            f.bias.empty() != f0.bias.empty() || f.bz.empty() != f0.bz.empty() || !f.parts.empty() ||
+            vals_[f.out].consumers.size() != 1 || is_requested(f.out) || vals_[f.out].minmax_slot >= 0)
+          ok = false;
+      }
+      if (!ok) continue;
+      int first = ids[0];
+      for (int t = 1; t < 3; ++t)
+        if (pos_of(ids[t]) < pos_of(first)) first = ids[t];
+      FusedQL m;
+      m.q = f0.q;
+      m.s = f0.s;
+      m.z = f0.z;
+      m.bias = f0.bias.empty() ? "" : "merged";
+      m.bz = f0.bz.empty() ? "" : "merged";
+      for (int t = 0; t < 3; ++t) m.parts.push_back(fused_[ids[t]]);
+      m.w = "qkv:" + m.parts[0].w + "|" + m.parts[1].w + "|" + m.parts[2].w;
+      m.out = a.q + "#qkv";
+      Val mv;
+      mv.dtype = ICX_F32;
+      mv.shape = vals_[a.q].shape;
+      const int64_t N = mv.shape.back();
+      mv.shape.back() = 3 * N;
+      mv.producer = first;
+      vals_[m.out] = mv;
+      for (int t = 0; t < 3; ++t) {
+        fused_.erase(ids[t]);
+        if (ids[t] != first) skip_.insert(ids[t]);
+      }
+      fused_[first] = m;
+      a.q = a.k = a.v = m.out;
+      a.ld = 3 * N;
+      a.off_q = 0;
+      a.off_k = N;
+      a.off_v = 2 * N;
+    }
+  }
+
   // ---------------------------------------------------- weights upload
   int upload_weights() {
     for (auto& kv : inits_) {
@@ -952,8 +1041,60 @@ class Engine {
       prepared_[wname] = p;
       return ICX_OK;
     };
+    for (auto& kv : fused_) {
+      const FusedQL& f = kv.second;
+      if (f.parts.empty()) {
+        int rc = prep(f.w);
+        if (rc) return rc;
+        continue;
+      }
+      if (prepared_.count(f.w)) continue;
+      Prepared m;
+      m.K = init_of(f.parts[0].w)->shape[0];
+      for (auto& part : f.parts) {
+        int rc = prep(part.w);
+        if (rc) return rc;
+        m.N += prepared_[part.w].N;
+      }
+      ICX_CUDA(cudaMalloc(&m.bt, (size_t)(m.K * m.N) + 16));
+      ICX_CUDA(cudaMalloc(&m.colsum, (size_t)m.N * 4 + 16));
+      std::vector<float> ws, bias;
+      std::vector<int8_t> bz;
+      int64_t n0 = 0;
+      for (auto& part : f.parts) {
+        const Prepared& p = prepared_[part.w];
+        ICX_CUDA(cudaMemcpy(static_cast<uint8_t*>(m.bt) + n0 * m.K, p.bt, (size_t)(p.N * p.K),
+                            cudaMemcpyDeviceToDevice));
+        ICX_CUDA(cudaMemcpy(m.colsum + n0, p.colsum, (size_t)p.N * 4, cudaMemcpyDeviceToDevice));
+        const Init* wsi = init_of(part.ws);
+        for (int64_t j = 0; j < p.N; ++j)
+          ws.push_back(reinterpret_cast<const float*>(wsi->data.data())[numel(wsi->shape) > 1 ? j : 0]);
+        if (!part.bias.empty()) {
+          const Init* bi = init_of(part.bias);
+          const float* bp = reinterpret_cast<const float*>(bi->data.data());
+          bias.insert(bias.end(), bp, bp + p.N);
+        }
+        if (!part.bz.empty()) {
+          const Init* zi = init_of(part.bz);
+          for (int64_t j = 0; j < p.N; ++j)
+            bz.push_back(reinterpret_cast<const int8_t*>(zi->data.data())[numel(zi->shape) > 1 ? j : 0]);
+        }
+        n0 += p.N;
+      }
+      ICX_CUDA(cudaMalloc(&m.ws, ws.size() * 4));
+      ICX_CUDA(cudaMemcpy(m.ws, ws.data(), ws.size() * 4, cudaMemcpyHostToDevice));
+      if (!bias.empty()) {
+        ICX_CUDA(cudaMalloc(&m.bias, bias.size() * 4));
+        ICX_CUDA(cudaMemcpy(m.bias, bias.data(), bias.size() * 4, cudaMemcpyHostToDevice));
+      }
+      if (!bz.empty()) {
+        ICX_CUDA(cudaMalloc(&m.bz, bz.size() + 16));
+        ICX_CUDA(cudaMemcpy(m.bz, bz.data(), bz.size(), cudaMemcpyHostToDevice));
+      }
+      prepared_[f.w] = m;
+    }
     for (int idx : order_) {
-      if (skip_.count(idx)) continue;
+      if (skip_.count(idx) || fused_.count(idx)) continue;
       const NodeDef& n = nodes_[idx];
       if (n.op == "MatMulInteger") {
         const Init* w = init_of(n.in[1]);
@@ -994,7 +1135,8 @@ class Engine {
         // the quantised input, scale and zero point at this position
         const FusedQL& f = fit->second;
         if (!life.count(f.out)) life[f.out] = {pos, pos};
-        for (const std::string* i : {&f.q, &f.s, &f.z}) {
+        for (const std::string* i : {&f.q, &f.s, &f.z, &f.residual}) {
+          if (i->empty()) continue;
           const std::string r = root(*i);
           auto it = life.find(r);
           if (it != life.end()) it->second.second = std::max(it->second.second, pos);
@@ -1003,7 +1145,7 @@ class Engine {
       auto ait = attn_.find(idx);
       if (ait != attn_.end()) {
         const FusedAttn& at = ait->second;
-        if (!life.count(at.scores)) life[at.scores] = {pos, pos};
+        if (vals_[at.scores].needed && !life.count(at.scores)) life[at.scores] = {pos, pos};
         for (const std::string* i : {&at.q, &at.k, &at.v, &at.mask}) {
           if (i->empty()) continue;
           const std::string r = root(*i);
@@ -1107,9 +1249,10 @@ class Engine {
     const Val& q = vals_[f.q];
     const int64_t K = q.shape.back();
     const int64_t M = numel(q.shape) / (K ? K : 1);
-    const Init* ws = init_of(f.ws);
-    const Init* bz = f.bz.empty() ? nullptr : init_of(f.bz);
-    const Init* bias = f.bias.empty() ? nullptr : init_of(f.bias);
+    const bool merged = !f.parts.empty();
+    const Init* ws = merged ? nullptr : init_of(f.ws);
+    const Init* bz = merged || f.bz.empty() ? nullptr : init_of(f.bz);
+    const Init* bias = merged || f.bias.empty() ? nullptr : init_of(f.bias);
     uint8_t* qp = static_cast<uint8_t*>(resolve(f.q));
     float* sp = static_cast<float*>(resolve(f.s));
     uint8_t* zp = static_cast<uint8_t*>(resolve(f.z));
@@ -1117,18 +1260,23 @@ class Engine {
     const int slot = vals_[f.out].minmax_slot;
     float* mm = slot >= 0 ? slot_ptr(slot) : nullptr;
     int* mmc = slot >= 0 ? &minmax_count_[slot] : nullptr;
-    const int32_t* rows = bz ? rowsum_for(f.q, M) : nullptr;
+    const bool has_bz = !f.bz.empty();
+    const int32_t* rows = has_bz ? rowsum_for(f.q, M) : nullptr;
     const bool gelu = f.gelu;
-    const float* wsp = static_cast<const float*>(ws->dev);
-    const int ws_pc = numel(ws->shape) > 1;
-    const int8_t* bzp = bz ? static_cast<const int8_t*>(bz->dev) : nullptr;
-    const int bz_pc = bz && numel(bz->shape) > 1;
-    const float* bp = bias ? static_cast<const float*>(bias->dev) : nullptr;
+    const float* wsp = merged ? p.ws : static_cast<const float*>(ws->dev);
+    const int ws_pc = merged ? 1 : numel(ws->shape) > 1;
+    const int8_t* bzp = merged ? p.bz : (bz ? static_cast<const int8_t*>(bz->dev) : nullptr);
+    const int bz_pc = merged ? 1 : (bz && numel(bz->shape) > 1);
+    const float* bp = merged ? p.bias : (bias ? static_cast<const float*>(bias->dev) : nullptr);
     Prepared pw = p;
-    add_step(n, gelu ? "QuantLinear+GELU" : "QuantLinear", f.out, [=](cudaStream_t s) {
+    const float* res = f.residual.empty() ? nullptr : static_cast<const float*>(resolve(f.residual));
+    const std::string label = gelu ? "QuantLinear+GELU"
+                              : res ? "QuantLinear+Residual"
+                              : merged ? "QuantLinear(QKV)" : "QuantLinear";
+    add_step(n, label, f.out, [=](cudaStream_t s) {
       return icx_quant_linear(s, qp, sp, zp, rows, static_cast<const int8_t*>(pw.bt), pw.colsum,
                               (size_t)M, (size_t)K, (size_t)pw.N, wsp, ws_pc, bzp, bz_pc, bp,
-                              gelu ? 1 : 0, out, mm, mmc);
+                              gelu ? 1 : 0, res, out, mm, mmc);
     }, 1);
     return ICX_OK;
   }
@@ -1139,6 +1287,20 @@ class Engine {
   // applies Div(c), Add(mask) and Softmax with the rounding of those ops.
   int step_attention(int idx, const FusedAttn& a) {
     const NodeDef& n = nodes_[idx];
+    if (attention_supported(a.dh, a.ld ? a.ld : a.H, a.H)) {
+      const float* q = static_cast<const float*>(resolve(a.q)) + a.off_q;
+      const float* k = static_cast<const float*>(resolve(a.k)) + a.off_k;
+      const float* v = static_cast<const float*>(resolve(a.v)) + a.off_v;
+      float* out = static_cast<float*>(resolve(a.out));
+      const float* mask = a.mask.empty() ? nullptr : static_cast<const float*>(resolve(a.mask));
+      const FusedAttn at = a;
+      const int64_t ld = a.ld ? a.ld : a.H;
+      add_step(n, "Attention", a.out, [=](cudaStream_t s) {
+        return launch_attention_f32(s, q, k, v, ld, out, at.B, at.S, at.H, at.nh, at.c, mask,
+                                    at.mask_per_batch);
+      }, 1);
+      return ICX_OK;
+    }
     const int64_t nb = a.B * a.nh;
     std::vector<const float*> hA1(nb), hB1(nb), hA2(nb), hB2(nb);
     std::vector<float*> hC1(nb), hC2(nb);
@@ -1150,13 +1312,15 @@ class Engine {
     for (int64_t b = 0; b < a.B; ++b)
       for (int64_t h = 0; h < a.nh; ++h) {
         const int64_t i = b * a.nh + h;
-        const int64_t off = b * a.S * a.H + h * a.dh;
-        hA1[i] = k + off;
-        hB1[i] = q + off;
+        const int64_t ld = a.ld ? a.ld : a.H;
+        const int64_t in_off = b * a.S * ld + h * a.dh;
+        const int64_t out_off = b * a.S * a.H + h * a.dh;
+        hA1[i] = k + in_off + a.off_k;
+        hB1[i] = q + in_off + a.off_q;
         hC1[i] = sc + i * a.S * a.S;
-        hA2[i] = v + off;
+        hA2[i] = v + in_off + a.off_v;
         hB2[i] = sc + i * a.S * a.S;
-        hC2[i] = out + off;
+        hC2[i] = out + out_off;
       }
     void* dptr = nullptr;
     ICX_CUDA(cudaMalloc(&dptr, (size_t)nb * 6 * sizeof(void*)));
@@ -1171,14 +1335,15 @@ class Engine {
     ICX_CUDA(cudaMemcpy(d + 5 * nb, hC2.data(), pb, cudaMemcpyHostToDevice));
     const float* mask = a.mask.empty() ? nullptr : static_cast<const float*>(resolve(a.mask));
     const FusedAttn at = a;
+    const int64_t lda = a.ld ? a.ld : a.H;
     cublasHandle_t hdl = blas_;
     add_step(n, "Attention", a.out, [=](cudaStream_t s) {
       const float one = 1.0f, zero = 0.0f;
       // scores[b,h] (row-major S x S) = Q_bh K_bh^T
       cublasStatus_t st = cublasSgemmBatched(
           hdl, CUBLAS_OP_T, CUBLAS_OP_N, (int)at.S, (int)at.S, (int)at.dh, &one,
-          reinterpret_cast<const float* const*>(d + 0 * nb), (int)at.H,
-          reinterpret_cast<const float* const*>(d + 1 * nb), (int)at.H, &zero,
+          reinterpret_cast<const float* const*>(d + 0 * nb), (int)lda,
+          reinterpret_cast<const float* const*>(d + 1 * nb), (int)lda, &zero,
           reinterpret_cast<float* const*>(d + 2 * nb), (int)at.S, (int)nb);
       if (st != CUBLAS_STATUS_SUCCESS) {
         set_error("cublasSgemmBatched (scores) failed (%d)", (int)st);
@@ -1189,7 +1354,7 @@ class Engine {
       if (rc) return rc;
       // ctx[b, :, h*dh:(h+1)*dh] = P_bh V_bh
       st = cublasSgemmBatched(hdl, CUBLAS_OP_N, CUBLAS_OP_N, (int)at.dh, (int)at.S, (int)at.S, &one,
-                              reinterpret_cast<const float* const*>(d + 3 * nb), (int)at.H,
+                              reinterpret_cast<const float* const*>(d + 3 * nb), (int)lda,
                               reinterpret_cast<const float* const*>(d + 4 * nb), (int)at.S, &zero,
                               reinterpret_cast<float* const*>(d + 5 * nb), (int)at.H, (int)nb);
       if (st != CUBLAS_STATUS_SUCCESS) {

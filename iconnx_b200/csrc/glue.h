@@ -33,6 +33,12 @@ int launch_cast(cudaStream_t s, const void* x, int from, void* y, int to, size_t
 int launch_erf(cudaStream_t s, const float* x, float* y, size_t n);
 int launch_gelu(cudaStream_t s, const float* x, float* y, size_t n);
 
+// attention.cu
+bool attention_supported(int64_t dh, int64_t ld, int64_t H);
+int launch_attention_f32(cudaStream_t s, const float* q, const float* k, const float* v, int64_t ld,
+                         float* out, int64_t B, int64_t S, int64_t H, int64_t nh, float c,
+                         const float* mask, bool mask_per_batch);
+
 // dql.cu
 int dql_minmax_partials(size_t n);
 int launch_dql_minmax(cudaStream_t s, const float* x, size_t n, float2* partials);

@@ -57,6 +57,7 @@ struct GemmArgs {
   int w_scale_per_col;
   const float* bias;      // nullable, N
   void* out;              // s32 or f32 [M, N]
+  const float* residual;  // nullable: f32 [M, N] added after the bias (residual Add)
   float2* minmax;         // nullable: per-CTA (min, max) of the f32 output,
                           // seeded with 0 like DynamicQuantizeLinear's scan
 };
@@ -392,6 +393,24 @@ __global__ void __launch_bounds__(kThreads, 1)
             r[4 * q + 3] = finish1<EPI, HAS_BIAS>(v3, sc.w, bi.w);
           }
         }
+        if (EPI == kEpiF32 && args.residual != nullptr && m < M) {
+          // residual Add(out, r): one more separately rounded f32 addition
+          const float* rr = args.residual + (size_t)m * N + nb;
+          if (vec && nb + 32 <= N && ((reinterpret_cast<uintptr_t>(args.residual) & 15) == 0)) {
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              const float4 rv = __ldg(reinterpret_cast<const float4*>(rr) + q);
+              r[4 * q + 0] = __float_as_uint(__fadd_rn(__uint_as_float(r[4 * q + 0]), rv.x));
+              r[4 * q + 1] = __float_as_uint(__fadd_rn(__uint_as_float(r[4 * q + 1]), rv.y));
+              r[4 * q + 2] = __float_as_uint(__fadd_rn(__uint_as_float(r[4 * q + 2]), rv.z));
+              r[4 * q + 3] = __float_as_uint(__fadd_rn(__uint_as_float(r[4 * q + 3]), rv.w));
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (nb + j < N) r[j] = __float_as_uint(__fadd_rn(__uint_as_float(r[j]), rr[j]));
+          }
+        }
         if (track && m < M) {
           if (nb + 32 <= N) {
 #pragma unroll
@@ -498,6 +517,7 @@ __global__ void qgemm_simt_kernel(const void* __restrict__ a, int a_signed,
     float f = __fmul_rn(__int2float_rn(v), sc);
     if (args.bias) f = __fadd_rn(f, args.bias[n]);
     if (EPI == kEpiGelu) f = gelu_erf(f);
+    if (EPI == kEpiF32 && args.residual) f = __fadd_rn(f, args.residual[idx]);
     static_cast<float*>(args.out)[idx] = f;
   }
 }
@@ -798,7 +818,8 @@ extern "C" int icx_quant_linear(void* stream, const uint8_t* d_q,
                                 size_t N, const float* d_w_scale,
                                 int w_scale_per_col, const int8_t* d_b_zp,
                                 int b_zp_per_col, const float* d_bias, int gelu,
-                                float* d_out, float* d_minmax, int* n_minmax) {
+                                const float* d_residual, float* d_out, float* d_minmax,
+                                int* n_minmax) {
   ICX_REQUIRE(M < (1u << 31) && N < (1u << 30) && K < (1u << 30),
               "QuantLinear: shape too large");
   if (M == 0 || N == 0) return ICX_OK;
@@ -814,6 +835,7 @@ extern "C" int icx_quant_linear(void* stream, const uint8_t* d_q,
   g.colsum = d_colsum; g.rowsum = d_rowsum_q;
   g.a_scale = d_a_scale; g.w_scale = d_w_scale; g.w_scale_per_col = w_scale_per_col;
   g.bias = d_bias;
+  g.residual = d_residual;
   g.out = d_out;
   g.minmax = reinterpret_cast<float2*>(d_minmax);
   if (n_minmax) *n_minmax = gemm_grid(g, d_q, d_wt);

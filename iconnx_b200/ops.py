@@ -191,7 +191,8 @@ def quant_linear(q: torch.Tensor, a_scale: torch.Tensor, a_zp: torch.Tensor, w: 
                  w_scale: torch.Tensor, bias: torch.Tensor | None = None,
                  b_zp: torch.Tensor | None = None, rowsum: torch.Tensor | None = None,
                  gelu: bool = False, out: torch.Tensor | None = None,
-                 minmax: "MinMaxPartials | None" = None) -> torch.Tensor:
+                 minmax: "MinMaxPartials | None" = None,
+                 residual: torch.Tensor | None = None) -> torch.Tensor:
     """Fused MatMulInteger -> Cast -> Mul(a_scale*w_scale) -> Add(bias) [-> GELU].
 
     With ``minmax`` the kernel also records (min, max) partials of the output
@@ -207,7 +208,7 @@ def quant_linear(q: torch.Tensor, a_scale: torch.Tensor, a_zp: torch.Tensor, w: 
     per_col_z = int(b_zp is not None and b_zp.numel() > 1)
     check(_lib.load().icx_quant_linear(
         _stream(q), _ptr(q), _ptr(a_scale), _ptr(a_zp), _ptr(rowsum), _ptr(w.bt), _ptr(w.colsum),
-        M, K, w.N, _ptr(w_scale), per_col_s, _ptr(b_zp), per_col_z, _ptr(bias), int(gelu), _ptr(out),
+        M, K, w.N, _ptr(w_scale), per_col_s, _ptr(b_zp), per_col_z, _ptr(bias), int(gelu), _ptr(residual), _ptr(out),
         None if minmax is None else minmax.buf.data_ptr(),
         None if minmax is None else ctypes.byref(minmax.count)))
     return out

@@ -176,6 +176,8 @@ ICX_API int icx_matmul_integer_prepared(void* stream, const void* d_a, int a_typ
  * outputs; wt/colsum: prepared weight; w_scale: 1 or N floats; b_zp: NULL,
  * 1 or N s8 values; bias: N floats (or NULL); out: f32 [M, N].
  * The s32 accumulator never leaves the SM: it lives in tensor memory.
+ * d_residual (nullable, f32 [M, N], not with gelu): a following residual
+ * Add(out, residual) is applied in the epilogue, rounded separately.
  * d_minmax (nullable, room for ICX_MAX_MINMAX_PARTIALS float pairs): the
  * kernel also writes (min, max) partials of `out` (seeded with 0, NaN
  * skipped) so a following DynamicQuantizeLinear needs only its quantise
@@ -187,7 +189,8 @@ ICX_API int icx_quant_linear(void* stream, const uint8_t* d_q, const float* d_a_
                      size_t K, size_t N, const float* d_w_scale,
                      int w_scale_per_col, const int8_t* d_b_zp,
                      int b_zp_per_col, const float* d_bias, int gelu,
-                     float* d_out, float* d_minmax, int* n_minmax);
+                     const float* d_residual, float* d_out, float* d_minmax,
+                     int* n_minmax);
 
 /* ======================================================================== *
  * DequantizeLinear: y = (f32(x) - f32(zp)) * scale, per tensor or per axis.

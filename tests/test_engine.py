@@ -115,9 +115,11 @@ def test_encoder_matches_cpu_interpreter(cfg, batch, seq):
     assert np.mean(np.abs(g - r) > 1e-3) < 0.05  # quantisation-boundary flips
     plan = ex.plan()
     fused = [s for s in plan if s.startswith("QuantLinear")]
-    assert len(fused) == 6 * cfg.layers
+    assert len(fused) == 4 * cfg.layers          # Q/K/V share one merged GEMM
+    assert len([s for s in plan if s.startswith("QuantLinear(QKV)")]) == cfg.layers
     assert len([s for s in plan if s.startswith("Attention ")]) == cfg.layers
     assert not any(s.startswith(("Transpose", "Softmax", "MatMul ")) for s in plan)
+    assert len([s for s in plan if s.startswith("QuantLinear+Residual")]) == 2 * cfg.layers
 
 
 @gpu

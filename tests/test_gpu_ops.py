@@ -332,3 +332,18 @@ def test_ffn_block_fused_chain_bit_exact():
     np.testing.assert_array_equal(host(y2), ry2)
     assert host(s2).item() == rs2 and host(z2).item() == rz2
     np.testing.assert_array_equal(host(out).view(np.uint32), rout.view(np.uint32))
+
+
+def test_quant_linear_residual_epilogue_bit_exact():
+    """Residual Add(out, r) fused in the epilogue == the separate f32 Add."""
+    M, K, N = 1000, 768, 768
+    x = synth.normal((M, K), 1.0, 41)
+    r = synth.normal((M, N), 3.0, 42)
+    w = synth.int8_uniform((K, N), 43)
+    bias = synth.normal((N,), 0.02, 44)
+    ws = np.array([0.01], np.float32)
+    pw = ops.prepare_weight(cu(w))
+    y, s, z = ops.gpu_dynamic_quantize_linear(cu(x))
+    out = ops.quant_linear(y, s, z, pw, cu(ws), cu(bias), residual=cu(r))
+    ref = oracle.quant_linear(x, w, ws, bias)[0] + r
+    np.testing.assert_array_equal(host(out).view(np.uint32), ref.astype(np.float32).view(np.uint32))
