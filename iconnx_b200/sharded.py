@@ -1,0 +1,100 @@
+"""Batch-sharded multi-GPU inference: one executor per GPU.
+
+The reference has no multi-GPU code and its GpuGraphExecutor is !Sync and
+hard-wired to device 0 (src/cuda/context.rs:49-60).  Inference of the int8
+encoder shards by batch with no cross-GPU exchange, so the B200 design is one
+GpuGraphExecutor per device, each owned and driven by its own host thread, the
+batch split along axis 0 and the outputs concatenated on the host.  No NCCL
+collective is on the data path.
+
+Per-shard dynamic quantisation takes its min/max over the shard, so a sharded
+run equals, shard by shard, an independent executor on that sub-batch; it is
+not bit-equal to a single executor over the whole batch.
+
+A failing shard raises in the caller; a shard that does not finish within
+``timeout`` seconds raises TimeoutError without waiting for it.
+"""
+
+from __future__ import annotations
+
+import threading
+from typing import Callable
+
+import numpy as np
+
+
+def shard_bounds(n: int, shards: int) -> list[tuple[int, int]]:
+    """Contiguous [start, end) rows per shard, sizes differing by at most 1."""
+    base, extra = divmod(n, shards)
+    out, s = [], 0
+    for i in range(shards):
+        e = s + base + (1 if i < extra else 0)
+        out.append((s, e))
+        s = e
+    return out
+
+
+class ShardedRunner:
+    """Runs one graph on several devices, splitting every input along axis 0.
+
+    ``build(builder, batch)`` adds the graph for `batch` rows to a builder and
+    returns nothing; ``factory(device)`` returns an executor (default:
+    GpuGraphExecutor on that CUDA device).  Each executor is created, built and
+    run only on its own worker thread.
+    """
+
+    def __init__(self, build: Callable, devices: list, batch: int,
+                 factory: Callable | None = None):
+        if factory is None:
+            from .engine import GpuGraphExecutor
+            factory = GpuGraphExecutor.new
+        self.devices = list(devices)
+        self.bounds = [b for b in shard_bounds(batch, len(self.devices))]
+        self._build, self._factory = build, factory
+        self._ex = [None] * len(self.devices)
+
+    def _ensure(self, i):
+        if self._ex[i] is None:
+            ex = self._factory(self.devices[i])
+            s, e = self.bounds[i]
+            self._build(ex, e - s)
+            self._ex[i] = ex
+        return self._ex[i]
+
+    def run(self, inputs: dict, outputs, timeout: float | None = None) -> dict:
+        n = len(self.devices)
+        results: list = [None] * n
+        errors: list = [None] * n
+
+        def work(i):
+            try:
+                ex = self._ensure(i)
+                s, e = self.bounds[i]
+                results[i] = ex.run({k: v[s:e] for k, v in inputs.items()}, outputs)
+            except BaseException as exc:  # propagated to the caller below
+                errors[i] = exc
+
+        threads = [threading.Thread(target=work, args=(i,), daemon=True) for i in range(n)
+                   if self.bounds[i][1] > self.bounds[i][0]]
+        for t in threads:
+            t.start()
+        for t in threads:
+            t.join(timeout)
+            if t.is_alive():
+                raise TimeoutError(f"a shard did not finish within {timeout} s")
+        for i, err in enumerate(errors):
+            if err is not None:
+                raise RuntimeError(f"shard {i} (device {self.devices[i]}) failed: {err}") from err
+        return {o: np.concatenate([r[o] for r in results if r is not None], axis=0) for o in outputs}
+
+
+def max_over_ranks(value: float, device=None) -> float:
+    """Max of a per-rank scalar over the default process group (timings are
+    reported as the slowest rank); identity without torch.distributed."""
+    import torch
+    import torch.distributed as dist
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size() == 1:
+        return float(value)
+    t = torch.tensor([float(value)], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
