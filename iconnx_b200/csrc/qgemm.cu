@@ -106,7 +106,8 @@ struct Cfg {
   static constexpr int kOutOffset = kStages * kStageBytes;
   static constexpr int kBarOffset = kOutOffset + kEpiWarps * kStageOutBytes;
   // barriers (2*stages + 4) * 8 B, the TMEM slot, 8 (min,max) pairs
-  static constexpr int kSmemBytes = kBarOffset + 256 + 1024 /*align slack*/;
+  static constexpr int kSmemBytes = kBarOffset + 512 + 1024 /*align slack*/;
+  // barriers, TMEM slot, (min, max) reduction slots, residual-load barriers
   static_assert((2 * kStages + 4) * 8 + 8 + kEpiWarps * 8 <= 256, "barrier area");
 };
 
@@ -161,7 +162,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     qgemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA,
                          const __grid_constant__ CUtensorMap tmB,
                          const __grid_constant__ CUtensorMap tmOut,
-                         const GemmArgs args, uint32_t idesc, int tma_store, int vec_cols) {
+                         const __grid_constant__ CUtensorMap tmRes,
+                         const GemmArgs args, uint32_t idesc, int tma_store, int vec_cols,
+                         int tma_res) {
   using C = Cfg<BN>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -175,6 +178,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* tfull = bars + 2 * C::kStages;
   uint64_t* tempty = tfull + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  // residual tile barriers, one per epilogue warp
+  uint64_t* rbar = reinterpret_cast<uint64_t*>(smem + C::kBarOffset + 256);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -193,6 +198,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&tfull[a], 1);
       mbar_init(&tempty[a], kEpiWarps);
     }
+    for (int w = 0; w < kEpiWarps; ++w) mbar_init(&rbar[w], 1);
     fence_barrier_init();
     fence_proxy_async_smem();
   }
@@ -200,6 +206,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
     if (tma_store) tma_prefetch_desc(&tmOut);
+    if (tma_res) tma_prefetch_desc(&tmRes);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, C::kTmemCols);
@@ -294,6 +301,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;  // false once a bounded wait gave up: skip work
     const bool track = (EPI != kEpiS32) && args.minmax != nullptr;
     float run_mn = 0.0f, run_mx = 0.0f;  // the DynamicQuantizeLinear seed
+    uint32_t rphase = 0;                 // parity of this warp's residual barrier
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
       const int m0 = (t / num_n) * kBM;
       const int n0 = (t % num_n) * BN;
@@ -322,6 +330,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int nb = n0 + c * 32;
         if (nb >= N) break;  // warp-uniform
         const bool fast = vec && (nb + 32 <= N) && !(HAS_BZ && bz_per_col);
+        const bool res_tma = EPI == kEpiF32 && tma_res && mrow0 < M;
+        if (res_tma && lane == 0) {
+          // residual box -> this warp's staging buffer, overlapped with the math
+          bulk_wait_read0();
+          mbar_arrive_expect_tx(&rbar[e], kStageOutBytes);
+          tma_load_2d(stage_out, &tmRes, &rbar[e], nb, mrow0);
+        }
         uint32_t r[32];
         tmem_ld_32x32b_x32(t_row + (uint32_t)(c * 32), r);
         tmem_ld_wait();
@@ -393,7 +408,21 @@ __global__ void __launch_bounds__(kThreads, 1)
             r[4 * q + 3] = finish1<EPI, HAS_BIAS>(v3, sc.w, bi.w);
           }
         }
-        if (EPI == kEpiF32 && args.residual != nullptr && m < M) {
+        if (res_tma) {
+          // residual Add(out, r) from the swizzled staging copy of the box
+          if (!mbar_wait(&rbar[e], rphase, ICX_DEVICE_TIMEOUT_EPILOGUE)) ok = false;
+          rphase ^= 1;
+          const uint8_t* rrow = stage_out + lane * 128;
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const float4 rv = *reinterpret_cast<const float4*>(rrow + ((q ^ (lane & 7)) << 4));
+            r[4 * q + 0] = __float_as_uint(__fadd_rn(__uint_as_float(r[4 * q + 0]), rv.x));
+            r[4 * q + 1] = __float_as_uint(__fadd_rn(__uint_as_float(r[4 * q + 1]), rv.y));
+            r[4 * q + 2] = __float_as_uint(__fadd_rn(__uint_as_float(r[4 * q + 2]), rv.z));
+            r[4 * q + 3] = __float_as_uint(__fadd_rn(__uint_as_float(r[4 * q + 3]), rv.w));
+          }
+          __syncwarp();  // every lane has read its row before it is overwritten
+        } else if (EPI == kEpiF32 && args.residual != nullptr && m < M) {
           // residual Add(out, r): one more separately rounded f32 addition
           const float* rr = args.residual + (size_t)m * N + nb;
           if (vec && nb + 32 <= N && ((reinterpret_cast<uintptr_t>(args.residual) & 15) == 0)) {
@@ -429,7 +458,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (tma_store) {
           if (mrow0 < M) {
             // the previous box of this warp must have been read out of smem
-            if (lane == 0) bulk_wait_read0();
+            if (lane == 0 && !res_tma) bulk_wait_read0();
             __syncwarp();
             uint8_t* row = stage_out + lane * 128;
 #pragma unroll
@@ -617,6 +646,13 @@ static int launch_tc(cudaStream_t s, const void* a, bool a_signed, const void* b
   } else {
     memset(&tout, 0, sizeof(tout));
   }
+  CUtensorMap tres;
+  memset(&tres, 0, sizeof(tres));
+  const int tma_res = tma_store && EPI == kEpiF32 && args.residual != nullptr && aligned16(args.residual);
+  if (tma_res) {
+    rc = make_out_tmap(&tres, const_cast<float*>(args.residual), (size_t)args.M, (size_t)args.N, true);
+    if (rc) return rc;
+  }
   const int vec_cols = (args.N % 4 == 0) && aligned16(args.colsum) &&
                        (args.w_scale == nullptr || !args.w_scale_per_col || aligned16(args.w_scale)) &&
                        (args.bias == nullptr || aligned16(args.bias));
@@ -630,7 +666,8 @@ static int launch_tc(cudaStream_t s, const void* a, bool a_signed, const void* b
   int grid = sm_count();
   if (ntiles < grid) grid = ntiles;
   const uint32_t idesc = idesc_i8(kBM, BN, a_signed, b_signed);
-  kern<<<grid, kThreads, C::kSmemBytes, s>>>(ta, tb, tout, args, idesc, tma_store, vec_cols);
+  kern<<<grid, kThreads, C::kSmemBytes, s>>>(ta, tb, tout, tres, args, idesc, tma_store, vec_cols,
+                                             tma_res);
   ICX_LAUNCH_CHECK();
   return ICX_OK;
 }
