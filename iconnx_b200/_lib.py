@@ -10,7 +10,7 @@ import ctypes
 import os
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-SO_PATH = os.path.join(HERE, "libiconnx_b200.so")
+SO_PATH = os.environ.get("ICONNX_B200_LIB") or os.path.join(HERE, "libiconnx_b200.so")
 HEADER = os.path.join(os.path.dirname(HERE), "include", "iconnx_b200.h")
 
 ICX_OK = 0

@@ -79,6 +79,43 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: the thread sleeps in hardware until the
+// phase completes or ~1 ms passes, instead of spinning on the barrier.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity), "r"(1000000u)
+      : "memory");
+  return ok != 0;
+}
+
+// Warp-collective bounded wait: lane 0 waits (sleeping in hardware), the
+// other lanes wait for it at __syncwarp.  Returns the same result on every
+// lane.  For consumers whose 32 lanes all need the phase.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, int code) {
+  uint32_t ok = 1;
+  if ((threadIdx.x & 31) == 0) {
+    if (!mbar_try_wait(bar, parity)) {
+      const uint64_t t0 = globaltimer_ns();
+      ok = 0;
+      while (globaltimer_ns() - t0 < kWaitLimitNs) {
+        if (mbar_try_wait_sleep(bar, parity)) {
+          ok = 1;
+          break;
+        }
+      }
+      if (!ok) record_status(code);
+    }
+  }
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  __syncwarp();
+  return ok != 0;
+}
+
 // Bounded wait for the phase with the given parity to complete.  Returns
 // false (and records `code`) when the limit is reached.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,

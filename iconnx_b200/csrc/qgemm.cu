@@ -96,15 +96,22 @@ constexpr int kEpiWarps = 8;                       // 2 per TMEM lane quadrant
 constexpr int kThreads = 64 + 32 * kEpiWarps;        // producer + MMA + epilogue
 constexpr int kStageOutBytes = 32 * 32 * 4;          // one warp's 32x32 output box
 
-template <int BN>
+// DEEP (K >= 1536): the main loop dominates, so keep a deep stage ring and
+// read per-column operands from global memory (L1-prefetched).  Otherwise
+// one stage fewer pays for staging those operands in shared memory, where the
+// epilogue (the bottleneck at small K) reads them with broadcast loads.
+template <int BN, bool DEEP = false>
 struct Cfg {
-  static constexpr int kStages = BN == 256 ? 4 : 6;
+  static constexpr int kStages = BN == 256 ? (DEEP ? 4 : 3) : (DEEP ? 6 : 5);
   static constexpr int kABytes = kBM * kBK;
   static constexpr int kBBytes = BN * kBK;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kTmemCols = 2 * BN;
   static constexpr int kOutOffset = kStages * kStageBytes;
-  static constexpr int kBarOffset = kOutOffset + kEpiWarps * kStageOutBytes;
+  // per-tile column operands (colsum, a_scale*w_scale, bias), double-buffered
+  static constexpr int kParamOffset = kOutOffset + kEpiWarps * kStageOutBytes;
+  static constexpr int kParamBytes = DEEP ? 0 : 2 * 3 * BN * 4;
+  static constexpr int kBarOffset = kParamOffset + kParamBytes;
   // barriers (2*stages + 4) * 8 B, the TMEM slot, 8 (min,max) pairs
   static constexpr int kSmemBytes = kBarOffset + 512 + 1024 /*align slack*/;
   // barriers, TMEM slot, (min, max) reduction slots, residual-load barriers
@@ -135,6 +142,94 @@ __device__ __forceinline__ void bulk_wait0() {
   asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
 
+// Packed fp32 pairs (sm_100 f32x2 instructions).  Used only inside the GELU,
+// whose contract is a tolerance: ptxas may contract a packed multiply and a
+// following packed add into an FMA even with .rn, so the bit-exact
+// dequantisation uses scalar __fmul_rn / __fadd_rn instead.
+__device__ __forceinline__ uint64_t pk(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void upk(uint64_t r, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t sub2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+
+// The GELU of gelu_erf on a pair of values with packed arithmetic.
+__device__ __forceinline__ uint64_t gelu_erf2(uint64_t x) {
+  const uint64_t u = mul2(x, pk(0.8493217825889587f, 0.8493217825889587f));
+  float u0, u1;
+  upk(u, u0, u1);
+  const uint64_t den = fma2(pk(0.2727374732494354f, 0.2727374732494354f), pk(fabsf(u0), fabsf(u1)),
+                            pk(1.0f, 1.0f));
+  float d0, d1, t0, t1, e0, e1;
+  upk(den, d0, d1);
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t0) : "f"(d0));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t1) : "f"(d1));
+  const uint64_t uu = mul2(u, u);
+  float q0, q1;
+  upk(uu, q0, q1);
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e0) : "f"(-q0));
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e1) : "f"(-q1));
+  const uint64_t t = pk(t0, t1);
+  uint64_t p = fma2(pk(0.5307027f, 0.5307027f), t, pk(-0.72657605f, -0.72657605f));
+  p = fma2(p, t, pk(0.7107069f, 0.7107069f));
+  p = fma2(p, t, pk(-0.14224836f, -0.14224836f));
+  p = fma2(p, t, pk(0.1274148f, 0.1274148f));
+  const uint64_t hq = mul2(mul2(p, t), pk(e0, e1));
+  const uint64_t xq = mul2(x, hq);
+  const uint64_t xm = sub2(x, xq);
+  float a0, a1, b0, b1;
+  upk(xm, a0, a1);
+  upk(xq, b0, b1);
+  return pk(u0 >= 0.0f ? a0 : b0, u1 >= 0.0f ? a1 : b1);
+}
+
+// Dequantise (and bias / GELU) two corrected accumulators at once.
+template <int EPI, bool HAS_BIAS>
+__device__ __forceinline__ void finish2(int32_t v0, int32_t v1, float s0, float s1, float b0,
+                                        float b1, uint32_t& o0, uint32_t& o1) {
+  if (EPI == kEpiS32) {
+    o0 = (uint32_t)v0;
+    o1 = (uint32_t)v1;
+    return;
+  }
+  // The dequantisation must stay two separately rounded scalar operations:
+  // ptxas contracts a packed mul.rn.f32x2 + add.rn.f32x2 pair into an FMA,
+  // which would break bit-exactness with the reference's Mul then Add.
+  float f0 = __fmul_rn(__int2float_rn(v0), s0), f1 = __fmul_rn(__int2float_rn(v1), s1);
+  if (HAS_BIAS) {
+    f0 = __fadd_rn(f0, b0);
+    f1 = __fadd_rn(f1, b1);
+  }
+  uint64_t f = pk(f0, f1);
+  if (EPI == kEpiGelu) f = gelu_erf2(f);  // tolerance-bound: packed FMAs are fine here
+  float a, b;
+  upk(f, a, b);
+  o0 = __float_as_uint(a);
+  o1 = __float_as_uint(b);
+}
+
 template <int EPI, bool HAS_BIAS>
 __device__ __forceinline__ uint32_t finish1(int32_t v, float sc, float bi) {
   if (EPI == kEpiS32) return (uint32_t)v;
@@ -157,7 +252,7 @@ __device__ __forceinline__ float4 ld4f(const float* p, int n, int N, bool vec) {
                      n + 3 < N ? p[n + 3] : 0.f);
 }
 
-template <int BN, int EPI, bool HAS_BZ, bool HAS_BIAS>
+template <int BN, int EPI, bool HAS_BZ, bool HAS_BIAS, bool DEEP>
 __global__ void __launch_bounds__(kThreads, 1)
     qgemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA,
                          const __grid_constant__ CUtensorMap tmB,
@@ -165,7 +260,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                          const __grid_constant__ CUtensorMap tmRes,
                          const GemmArgs args, uint32_t idesc, int tma_store, int vec_cols,
                          int tma_res) {
-  using C = Cfg<BN>;
+  using C = Cfg<BN, DEEP>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -302,6 +397,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool track = (EPI != kEpiS32) && args.minmax != nullptr;
     float run_mn = 0.0f, run_mx = 0.0f;  // the DynamicQuantizeLinear seed
     uint32_t rphase = 0;                 // parity of this warp's residual barrier
+    int tile_iter = 0;                   // selects the column-operand buffer
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
       const int m0 = (t / num_n) * kBM;
       const int n0 = (t % num_n) * BN;
@@ -309,11 +405,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int m = mrow0 + lane;
       uint32_t kza_rs = 0;
       if (HAS_BZ) kza_rs = (uint32_t)K * za - ((m < M) ? (uint32_t)args.rowsum[m] : 0u);
-      // pull this tile's per-column operands into L1 while the MMA runs
-      {
+      // stage this tile's per-column operands in shared memory while the MMA
+      // runs (double-buffered by tile parity; one epilogue barrier per tile)
+      int32_t* p_cs = reinterpret_cast<int32_t*>(smem + C::kParamOffset) + (tile_iter & 1) * 3 * BN;
+      float* p_sc = reinterpret_cast<float*>(p_cs + BN);
+      float* p_bi = p_sc + BN;
+      if (DEEP) {
+        // per-column operands come from global memory: pull them into L1
         const int et = threadIdx.x - 64;
-        const int lines = BN * 4 / 128;  // 128-byte lines per operand array
-        if (et < lines) {
+        if (et < BN * 4 / 128) {
           const int n = n0 + et * 32;
           if (n < N) {
             asm volatile("prefetch.global.L1 [%0];" ::"l"(args.colsum + n));
@@ -322,14 +422,29 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      if (ok) ok = mbar_wait(&tfull[acc], acc_phase, ICX_DEVICE_TIMEOUT_EPILOGUE);
+      for (int j = threadIdx.x - 64; !DEEP && j < BN; j += 32 * kEpiWarps) {
+        const int n = n0 + j;
+        int32_t cs = 0;
+        float sc = sc_scalar, bi = 0.0f;
+        if (n < N) {
+          cs = __ldg(args.colsum + n);
+          if (EPI != kEpiS32 && sc_per_col) sc = __fmul_rn(a_scale, __ldg(args.w_scale + n));
+          if (EPI != kEpiS32 && HAS_BIAS) bi = __ldg(args.bias + n);
+        }
+        p_cs[j] = cs;
+        p_sc[j] = sc;
+        p_bi[j] = bi;
+      }
+      if (!DEEP) epi_sync();
+      ++tile_iter;
+      if (ok) ok = mbar_wait_warp(&tfull[acc], acc_phase, ICX_DEVICE_TIMEOUT_EPILOGUE);
       tc_fence_after();
       const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
 #pragma unroll 1
       for (int c = part; c < BN / 32 && ok; c += kParts) {
         const int nb = n0 + c * 32;
         if (nb >= N) break;  // warp-uniform
-        const bool fast = vec && (nb + 32 <= N) && !(HAS_BZ && bz_per_col);
+        const bool fast = (DEEP ? vec : true) && (nb + 32 <= N) && !(HAS_BZ && bz_per_col);
         const bool res_tma = EPI == kEpiF32 && tma_res && mrow0 < M;
         if (res_tma && lane == 0) {
           // residual box -> this warp's staging buffer, overlapped with the math
@@ -342,20 +457,29 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld_wait();
         if (fast) {
           // whole chunk in range, 16-byte aligned operand vectors
-          const int4* cs4 = reinterpret_cast<const int4*>(args.colsum + nb);
-          const float4* bi4 = reinterpret_cast<const float4*>(args.bias + nb);
-          const float4* ws4 = reinterpret_cast<const float4*>(args.w_scale + nb);
+          const int4* cs4 = reinterpret_cast<const int4*>(p_cs + c * 32);
+          const float4* sc4 = reinterpret_cast<const float4*>(p_sc + c * 32);
+          const float4* bi4 = reinterpret_cast<const float4*>(p_bi + c * 32);
+          if (DEEP) {
+            cs4 = reinterpret_cast<const int4*>(args.colsum + nb);
+            sc4 = reinterpret_cast<const float4*>(args.w_scale + nb);
+            bi4 = reinterpret_cast<const float4*>(args.bias + nb);
+          }
 #pragma unroll
           for (int q = 0; q < 8; ++q) {
-            const int4 cs = __ldg(cs4 + q);
+            const int4 cs = DEEP ? __ldg(cs4 + q) : cs4[q];
             float4 sc = make_float4(sc_scalar, sc_scalar, sc_scalar, sc_scalar);
             if (EPI != kEpiS32 && sc_per_col) {
-              const float4 w = __ldg(ws4 + q);
-              sc = make_float4(__fmul_rn(a_scale, w.x), __fmul_rn(a_scale, w.y),
-                               __fmul_rn(a_scale, w.z), __fmul_rn(a_scale, w.w));
+              if (DEEP) {
+                const float4 w = __ldg(sc4 + q);
+                sc = make_float4(__fmul_rn(a_scale, w.x), __fmul_rn(a_scale, w.y),
+                                 __fmul_rn(a_scale, w.z), __fmul_rn(a_scale, w.w));
+              } else {
+                sc = sc4[q];
+              }
             }
             float4 bi = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (EPI != kEpiS32 && HAS_BIAS) bi = __ldg(bi4 + q);
+            if (EPI != kEpiS32 && HAS_BIAS) bi = DEEP ? __ldg(bi4 + q) : bi4[q];
             int32_t v0 = (int32_t)(r[4 * q + 0] - za * (uint32_t)cs.x);
             int32_t v1 = (int32_t)(r[4 * q + 1] - za * (uint32_t)cs.y);
             int32_t v2 = (int32_t)(r[4 * q + 2] - za * (uint32_t)cs.z);
@@ -367,10 +491,8 @@ __global__ void __launch_bounds__(kThreads, 1)
               v2 = (int32_t)((uint32_t)v2 + kb);
               v3 = (int32_t)((uint32_t)v3 + kb);
             }
-            r[4 * q + 0] = finish1<EPI, HAS_BIAS>(v0, sc.x, bi.x);
-            r[4 * q + 1] = finish1<EPI, HAS_BIAS>(v1, sc.y, bi.y);
-            r[4 * q + 2] = finish1<EPI, HAS_BIAS>(v2, sc.z, bi.z);
-            r[4 * q + 3] = finish1<EPI, HAS_BIAS>(v3, sc.w, bi.w);
+            finish2<EPI, HAS_BIAS>(v0, v1, sc.x, sc.y, bi.x, bi.y, r[4 * q + 0], r[4 * q + 1]);
+            finish2<EPI, HAS_BIAS>(v2, v3, sc.z, sc.w, bi.z, bi.w, r[4 * q + 2], r[4 * q + 3]);
           }
         } else {
 #pragma unroll
@@ -402,15 +524,13 @@ __global__ void __launch_bounds__(kThreads, 1)
               v2 = (int32_t)((uint32_t)v2 + kza_rs * (uint32_t)bz.z);
               v3 = (int32_t)((uint32_t)v3 + kza_rs * (uint32_t)bz.w);
             }
-            r[4 * q + 0] = finish1<EPI, HAS_BIAS>(v0, sc.x, bi.x);
-            r[4 * q + 1] = finish1<EPI, HAS_BIAS>(v1, sc.y, bi.y);
-            r[4 * q + 2] = finish1<EPI, HAS_BIAS>(v2, sc.z, bi.z);
-            r[4 * q + 3] = finish1<EPI, HAS_BIAS>(v3, sc.w, bi.w);
+            finish2<EPI, HAS_BIAS>(v0, v1, sc.x, sc.y, bi.x, bi.y, r[4 * q + 0], r[4 * q + 1]);
+            finish2<EPI, HAS_BIAS>(v2, v3, sc.z, sc.w, bi.z, bi.w, r[4 * q + 2], r[4 * q + 3]);
           }
         }
         if (res_tma) {
           // residual Add(out, r) from the swizzled staging copy of the box
-          if (!mbar_wait(&rbar[e], rphase, ICX_DEVICE_TIMEOUT_EPILOGUE)) ok = false;
+          if (!mbar_wait_warp(&rbar[e], rphase, ICX_DEVICE_TIMEOUT_EPILOGUE)) ok = false;
           rphase ^= 1;
           const uint8_t* rrow = stage_out + lane * 128;
 #pragma unroll
@@ -629,10 +749,10 @@ static int make_out_tmap(CUtensorMap* map, void* base, size_t M, size_t N, bool 
 
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
-template <int BN, int EPI>
+template <int BN, int EPI, bool DEEP>
 static int launch_tc(cudaStream_t s, const void* a, bool a_signed, const void* bt,
                      bool b_signed, const GemmArgs& args) {
-  using C = Cfg<BN>;
+  using C = Cfg<BN, DEEP>;
   CUtensorMap ta, tb, tout;
   int rc = make_tmap(&ta, a, (size_t)args.M, (size_t)args.K, kBM);
   if (rc) return rc;
@@ -656,10 +776,10 @@ static int launch_tc(cudaStream_t s, const void* a, bool a_signed, const void* b
   const int vec_cols = (args.N % 4 == 0) && aligned16(args.colsum) &&
                        (args.w_scale == nullptr || !args.w_scale_per_col || aligned16(args.w_scale)) &&
                        (args.bias == nullptr || aligned16(args.bias));
-  auto kern = args.b_zp ? (args.bias ? qgemm_tcgen05_kernel<BN, EPI, true, true>
-                                      : qgemm_tcgen05_kernel<BN, EPI, true, false>)
-                        : (args.bias ? qgemm_tcgen05_kernel<BN, EPI, false, true>
-                                     : qgemm_tcgen05_kernel<BN, EPI, false, false>);
+  auto kern = args.b_zp ? (args.bias ? qgemm_tcgen05_kernel<BN, EPI, true, true, DEEP>
+                                      : qgemm_tcgen05_kernel<BN, EPI, true, false, DEEP>)
+                        : (args.bias ? qgemm_tcgen05_kernel<BN, EPI, false, true, DEEP>
+                                     : qgemm_tcgen05_kernel<BN, EPI, false, false, DEEP>);
   ICX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 C::kSmemBytes));
   const int ntiles = ((args.M + kBM - 1) / kBM) * ((args.N + BN - 1) / BN);
@@ -703,8 +823,13 @@ static int launch_gemm(cudaStream_t s, const void* a, bool a_signed,
                        const void* bt, bool b_signed, const GemmArgs& args) {
   if (args.M == 0 || args.N == 0) return ICX_OK;
   const GemmPlan p = plan_gemm(args, a, bt);
-  if (p.bn == 256) return launch_tc<256, EPI>(s, a, a_signed, bt, b_signed, args);
-  if (p.bn == 128) return launch_tc<128, EPI>(s, a, a_signed, bt, b_signed, args);
+  const bool deep = args.K >= 1536;
+  if (p.bn == 256)
+    return deep ? launch_tc<256, EPI, true>(s, a, a_signed, bt, b_signed, args)
+                : launch_tc<256, EPI, false>(s, a, a_signed, bt, b_signed, args);
+  if (p.bn == 128)
+    return deep ? launch_tc<128, EPI, true>(s, a, a_signed, bt, b_signed, args)
+                : launch_tc<128, EPI, false>(s, a, a_signed, bt, b_signed, args);
   const size_t total = (size_t)args.M * args.N;
   const int threads = 256;
   const size_t blocks = (total + threads - 1) / threads;
