@@ -154,40 +154,59 @@ __device__ __forceinline__ uint32_t quant1(float xv, const DqlParams& p) {
   return quant_exact(xv, p.scale, p.zpf);
 }
 
-__device__ __forceinline__ uint32_t quant4(float4 v, const DqlParams& p,
-                                           uint32_t& sum) {
-  const uint32_t a = quant1(v.x, p), b = quant1(v.y, p), c = quant1(v.z, p),
-                 d = quant1(v.w, p);
-  sum += a + b + c + d;
+// Four elements at once.  Common case (finite scale, no element within 1e-4
+// of a half-integer): rintf, add the zero point, clamp to [0, 255] with
+// fminf/fmaxf (NaN -> 0), and read the integer out of the float's low byte
+// after adding 2^23; byte_perm packs the four bytes.  Otherwise every
+// element takes quant1 (with its exact f64 path where needed).
+template <bool SUM>
+__device__ __forceinline__ uint32_t quant4(float4 v, const DqlParams& p, uint32_t& sum) {
+  if (p.fast) {
+    const float t0 = v.x * p.inv32, t1 = v.y * p.inv32, t2 = v.z * p.inv32, t3 = v.w * p.inv32;
+    const float r0 = rintf(t0), r1 = rintf(t1), r2 = rintf(t2), r3 = rintf(t3);
+    const bool near = (fabsf(fabsf(t0 - r0) - 0.5f) <= 1e-4f) | (fabsf(fabsf(t1 - r1) - 0.5f) <= 1e-4f) |
+                      (fabsf(fabsf(t2 - r2) - 0.5f) <= 1e-4f) | (fabsf(fabsf(t3 - r3) - 0.5f) <= 1e-4f);
+    if (!near) {
+      const float q0 = fminf(fmaxf(r0 + p.zpf, 0.0f), 255.0f);
+      const float q1 = fminf(fmaxf(r1 + p.zpf, 0.0f), 255.0f);
+      const float q2 = fminf(fmaxf(r2 + p.zpf, 0.0f), 255.0f);
+      const float q3 = fminf(fmaxf(r3 + p.zpf, 0.0f), 255.0f);
+      if (SUM) sum += (uint32_t)((q0 + q1) + (q2 + q3));
+      const uint32_t b0 = __float_as_uint(q0 + 8388608.0f), b1 = __float_as_uint(q1 + 8388608.0f);
+      const uint32_t b2 = __float_as_uint(q2 + 8388608.0f), b3 = __float_as_uint(q3 + 8388608.0f);
+      return __byte_perm(__byte_perm(b0, b1, 0x0040), __byte_perm(b2, b3, 0x0040), 0x5410);
+    }
+  }
+  const uint32_t a = quant1(v.x, p), b = quant1(v.y, p), c = quant1(v.z, p), d = quant1(v.w, p);
+  if (SUM) sum += a + b + c + d;
   return a | (b << 8) | (c << 16) | (d << 24);
 }
 
-__global__ void __launch_bounds__(kQuantThreads, 4)
+__global__ void __launch_bounds__(kQuantThreads, 3)
     dql_quantize_kernel(const float* __restrict__ x, size_t n,
                         const float2* __restrict__ partials, int nparts,
                         uint8_t* __restrict__ y, float* __restrict__ scale_out,
                         uint8_t* __restrict__ zp_out,
                         int32_t* __restrict__ rowsum, size_t row_len,
                         int vec16) {
-  __shared__ DqlParams s_p;
+  // every warp folds the partials itself (no block barrier) and all lanes
+  // derive the f64 scale / zero point in parallel
+  DqlParams p;
   {
+    const int l = threadIdx.x & 31;
     float mn = 0.0f, mx = 0.0f;
-    for (int i = threadIdx.x; i < nparts; i += kQuantThreads) {
+    for (int i = l; i < nparts; i += 32) {
       const float2 v = partials[i];
       mn = fminf(mn, v.x);
       mx = fmaxf(mx, v.y);
     }
-    block_minmax<kQuantThreads>(mn, mx);
-    if (threadIdx.x == 0) {
-      s_p = dql_params(mn, mx);
-      if (blockIdx.x == 0) {
-        *scale_out = (float)s_p.scale;
-        *zp_out = (uint8_t)s_p.zpf;
-      }
+    warp_minmax(mn, mx);
+    p = dql_params(mn, mx);
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+      *scale_out = (float)p.scale;
+      *zp_out = (uint8_t)p.zpf;
     }
-    __syncthreads();
   }
-  const DqlParams p = s_p;
   const int lane = threadIdx.x & 31;
   const size_t warp_g = ((size_t)blockIdx.x * kQuantThreads + threadIdx.x) >> 5;
   const size_t nwarps = ((size_t)gridDim.x * kQuantThreads) >> 5;
@@ -221,8 +240,10 @@ __global__ void __launch_bounds__(kQuantThreads, 4)
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         uint32_t sum = 0;
-        y4[base4 + 32 * j + lane] = quant4(v[j], p, sum);
-        if (rowsum != nullptr) {
+        if (rowsum == nullptr) {
+          y4[base4 + 32 * j + lane] = quant4<false>(v[j], p, sum);
+        } else {
+          y4[base4 + 32 * j + lane] = quant4<true>(v[j], p, sum);
           const unsigned long long row =
               (unsigned long long)((base4 + 32 * j + lane) * 4 / row_len);
           const unsigned mask = __match_any_sync(0xffffffffu, row);
@@ -292,7 +313,7 @@ extern "C" int icx_dql_f32_u8(void* stream, const float* d_x, size_t n,
   size_t work = vec16 ? n / 16 : n;
   size_t qb = (work + kQuantThreads - 1) / kQuantThreads;
   if (qb < 1) qb = 1;
-  if (qb > 148 * 4) qb = 148 * 4;
+  if (qb > 148 * 3) qb = 148 * 3;
   dql_quantize_kernel<<<(int)qb, kQuantThreads, 0, s>>>(
       d_x, n, static_cast<const float2*>(d_workspace), blocks, d_y, d_scale,
       d_zp, d_rowsum, row_len ? row_len : 1, vec16);
@@ -319,7 +340,7 @@ extern "C" int icx_dql_quantize_f32_u8(void* stream, const float* d_x, size_t n,
   size_t work = vec16 ? n / 16 : n;
   size_t qb = (work + kQuantThreads - 1) / kQuantThreads;
   if (qb < 1) qb = 1;
-  if (qb > 148 * 4) qb = 148 * 4;
+  if (qb > 148 * 3) qb = 148 * 3;
   dql_quantize_kernel<<<(int)qb, kQuantThreads, 0, s>>>(
       d_x, n, reinterpret_cast<const float2*>(d_minmax), n_minmax, d_y, d_scale, d_zp,
       d_rowsum, row_len ? row_len : 1, vec16);
@@ -398,7 +419,7 @@ extern "C" int icx_dql_f32_u8_noalloc(void* stream, const float* d_x, size_t n,
   size_t work = vec16 ? n / 16 : n;
   size_t qb = (work + kQuantThreads - 1) / kQuantThreads;
   if (qb < 1) qb = 1;
-  if (qb > 148 * 4) qb = 148 * 4;
+  if (qb > 148 * 3) qb = 148 * 3;
   dql_quantize_kernel<<<(int)qb, kQuantThreads, 0, s>>>(
       d_x, n, scratch, blocks, d_y, d_scale, d_zp, d_rowsum, row_len ? row_len : 1, vec16);
   ICX_LAUNCH_CHECK();
