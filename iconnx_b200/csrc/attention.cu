@@ -12,10 +12,11 @@
 //
 // Layout: q / k / v rows are `ld` floats apart (the merged QKV GEMM output
 // has ld = 3H), head h occupies columns [h*dh, (h+1)*dh); ctx is [B, S, H].
-// Tiles: 256 threads; thread (ty, tx) = (tid / 16, tid % 16) owns score
-// rows ty + 16 i and key columns tx + 16 j (i, j < 4), and context columns
-// 4 tx .. 4 tx + 3.  Shared rows are padded to 68 floats so the strided
-// column pattern is bank-conflict free.
+// Tiles: 128 threads; thread (ty, tx) = (tid / 16, tid % 16) owns score
+// rows ty + 8 i (i < 8) and key columns tx + 16 j (j < 4), and context
+// columns 4 tx .. 4 tx + 3 of the same rows: 12 shared 16-byte loads per
+// 128 FMAs.  Shared rows are padded to 68 floats so the strided column
+// pattern is bank-conflict free.
 #include "capi.cuh"
 #include "common.cuh"
 #include "glue.h"
@@ -25,7 +26,15 @@ namespace icx {
 constexpr int kAttDh = 64;
 constexpr int kAttTile = 64;
 constexpr int kAttPad = 68;
-constexpr int kAttThreads = 256;
+constexpr int kAttThreads = 128;
+constexpr int kAttRows = 8;  // score / context rows per thread
+constexpr float kLog2e = 1.4426950408889634f;
+
+__device__ __forceinline__ float ex2f(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 
 __global__ void __launch_bounds__(kAttThreads)
     attention_f32_kernel(const float* __restrict__ q, const float* __restrict__ k,
@@ -43,6 +52,9 @@ __global__ void __launch_bounds__(kAttThreads)
   const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
   const size_t head = (size_t)b * S * ld + (size_t)h * kAttDh;
   const float* mrow = mask ? mask + (mask_per_batch ? (size_t)b * S : 0) : nullptr;
+  int cexp;
+  const bool c_pow2 = frexpf(c, &cexp) == 0.5f;
+  const float inv_c = 1.0f / c;
 
   // load the query tile (16 threads per 256-byte row)
   for (int r = tid >> 4; r < kAttTile; r += kAttThreads / 16) {
@@ -52,9 +64,9 @@ __global__ void __launch_bounds__(kAttThreads)
     *reinterpret_cast<float4*>(sQ + r * kAttPad + tx * 4) = val;
   }
 
-  float m_run[4], l_run[4], acc[4][4];
+  float m_run[kAttRows], l_run[kAttRows], acc[kAttRows][4];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
+  for (int i = 0; i < kAttRows; ++i) {
     m_run[i] = -INFINITY;
     l_run[i] = 0.0f;
 #pragma unroll
@@ -75,21 +87,21 @@ __global__ void __launch_bounds__(kAttThreads)
     }
     __syncthreads();
 
-    // scores for rows ty + 16 i, keys tx + 16 j
-    float s[4][4];
+    // scores for rows ty + 8 i, keys tx + 16 j
+    float s[kAttRows][4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
+    for (int i = 0; i < kAttRows; ++i)
 #pragma unroll
       for (int j = 0; j < 4; ++j) s[i][j] = 0.0f;
 #pragma unroll 4
     for (int d = 0; d < kAttDh; d += 4) {
-      float4 qa[4], ka[4];
+      float4 qa[kAttRows], ka[4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) qa[i] = *reinterpret_cast<const float4*>(sQ + (ty + 16 * i) * kAttPad + d);
+      for (int i = 0; i < kAttRows; ++i) qa[i] = *reinterpret_cast<const float4*>(sQ + (ty + 8 * i) * kAttPad + d);
 #pragma unroll
       for (int j = 0; j < 4; ++j) ka[j] = *reinterpret_cast<const float4*>(sK + (tx + 16 * j) * kAttPad + d);
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
+      for (int i = 0; i < kAttRows; ++i)
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           s[i][j] = fmaf(qa[i].x, ka[j].x, s[i][j]);
@@ -100,12 +112,14 @@ __global__ void __launch_bounds__(kAttThreads)
     }
     // Div(c), Add(mask), out-of-range keys -> -inf; online softmax update
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < kAttRows; ++i) {
       float rmax = -INFINITY;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const int key = k0 + tx + 16 * j;
-        float t = __fdiv_rn(s[i][j], c);
+        // Div(c): when c is a power of two, x * (1/c) is the same correctly
+        // rounded value as x / c, without the division sequence
+        float t = c_pow2 ? __fmul_rn(s[i][j], inv_c) : __fdiv_rn(s[i][j], c);
         if (mrow) t = __fadd_rn(t, key < S ? mrow[key] : 0.0f);
         if (key >= S) t = -INFINITY;
         s[i][j] = t;
@@ -114,11 +128,13 @@ __global__ void __launch_bounds__(kAttThreads)
 #pragma unroll
       for (int o = 8; o; o >>= 1) rmax = fmaxf(rmax, __shfl_xor_sync(0xffffffffu, rmax, o));
       const float m_new = fmaxf(m_run[i], rmax);
-      const float alpha = m_run[i] == -INFINITY ? 0.0f : expf(m_run[i] - m_new);
+      // exp(a - m) = 2^(a*log2e - m*log2e): one FMA and the hardware exp2
+      const float ml = m_new * kLog2e;
+      const float alpha = m_run[i] == -INFINITY ? 0.0f : ex2f(fmaf(m_run[i], kLog2e, -ml));
       float rsum = 0.0f;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const float p = s[i][j] == -INFINITY ? 0.0f : expf(s[i][j] - m_new);
+        const float p = s[i][j] == -INFINITY ? 0.0f : ex2f(fmaf(s[i][j], kLog2e, -ml));
         s[i][j] = p;
         rsum += p;
       }
@@ -129,19 +145,19 @@ __global__ void __launch_bounds__(kAttThreads)
 #pragma unroll
       for (int d = 0; d < 4; ++d) acc[i][d] *= alpha;
 #pragma unroll
-      for (int j = 0; j < 4; ++j) sP[(ty + 16 * i) * kAttPad + tx + 16 * j] = s[i][j];
+      for (int j = 0; j < 4; ++j) sP[(ty + 8 * i) * kAttPad + tx + 16 * j] = s[i][j];
     }
     __syncthreads();
     // acc[row][4 tx .. 4 tx + 3] += sum_key P[row][key] V[key][.]
 #pragma unroll 4
     for (int kk = 0; kk < kAttTile; kk += 4) {
-      float4 pa[4], va[4];
+      float4 pa[kAttRows], va[4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) pa[i] = *reinterpret_cast<const float4*>(sP + (ty + 16 * i) * kAttPad + kk);
+      for (int i = 0; i < kAttRows; ++i) pa[i] = *reinterpret_cast<const float4*>(sP + (ty + 8 * i) * kAttPad + kk);
 #pragma unroll
       for (int u = 0; u < 4; ++u) va[u] = *reinterpret_cast<const float4*>(sV + (kk + u) * kAttPad + tx * 4);
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
+      for (int i = 0; i < kAttRows; ++i) {
         const float pu[4] = {pa[i].x, pa[i].y, pa[i].z, pa[i].w};
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
@@ -154,8 +170,8 @@ __global__ void __launch_bounds__(kAttThreads)
     }
   }
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int qi = q0 + ty + 16 * i;
+  for (int i = 0; i < kAttRows; ++i) {
+    const int qi = q0 + ty + 8 * i;
     if (qi >= S) continue;
     const float inv = 1.0f / l_run[i];
     *reinterpret_cast<float4*>(out + ((size_t)b * S + qi) * H + (size_t)h * kAttDh + tx * 4) =
