@@ -46,6 +46,26 @@ sys.path.insert(0, ROOT)
 METRIC = "DistilBERT-int8 seq/s at 1/2/4/8 B200; MatMulInteger int8 TOPS vs peak"
 INT8_PEAK_TOPS = 4500.0  # B200 dense int8, datasheet (no measured int8 peak on this pool)
 
+# DRAM bytes (read + write) of one launch of the roofline kernel, from the ncu
+# captures summarised in profiles/ (cold cache).  The M=4096 x 768 x 3072 GELU
+# GEMM: profiles/qgemm_gelu_ffn1_M4096_K768_N3072.md.  The sweep kernel
+# (M=65536, K=N=4096) is too large to capture under the size rule: its value is
+# the M=8192 capture (profiles/qgemm_large_M8192_K4096_N4096.md) scaled by the
+# 8x rows, which is how its traffic grows (A and the output scale with M).
+TRAFFIC_FFN1_M4096 = 5.575168e6 + 0.987904e6
+TRAFFIC_SWEEP_FROM_M8192 = 8 * (50.599424e6 + 81.093632e6)
+
+
+def roofline_traffic(kdesc: str):
+    """ncu DRAM bytes per launch for the roofline kernel, scaled by rows."""
+    if "K=768 N=3072" in kdesc:
+        m = int(kdesc.split("M=")[1].split()[0])
+        return TRAFFIC_FFN1_M4096 * m / 4096
+    if "K=4096 N=4096" in kdesc:
+        m = int(kdesc.split("M=")[1].split()[0])
+        return TRAFFIC_SWEEP_FROM_M8192 * m / 65536
+    return None
+
 
 def load_peaks():
     try:
@@ -417,6 +437,39 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def run_kernel_probe(args):
+    """--kernel NAME: launch one kernel of the path a few times (for ncu
+    captures of a single kernel; prints no JSON line)."""
+    import torch
+    from iconnx_b200 import graphs, ops, synth
+    dev = torch.device("cuda", 0)
+    M, K, N = [int(v) for v in args.shape.split(",")]
+    if args.kernel in ("ffn1", "gemm", "quant", "residual"):
+        x = torch.from_numpy(synth.normal((M, K), 1.0, 0)).to(dev)
+        w = ops.prepare_weight(torch.from_numpy(synth.int8_uniform((K, N), 1)).to(dev))
+        b = torch.from_numpy(synth.normal((N,), 0.02, 2)).to(dev)
+        ws = torch.tensor([0.01], dtype=torch.float32, device=dev)
+        res = torch.from_numpy(synth.normal((M, N), 1.0, 5)).to(dev) if args.kernel == "residual" else None
+        y, s, z = ops.gpu_dynamic_quantize_linear(x)
+        out = torch.empty((M, N), dtype=torch.float32, device=dev)
+        mm = ops.MinMaxPartials(dev)
+        for _ in range(3):
+            ops.quant_linear(y, s, z, w, ws, b, gelu=args.kernel == "ffn1", out=out,
+                             minmax=mm if args.kernel == "quant" else None, residual=res)
+            if args.kernel == "quant":
+                ops.gpu_dynamic_quantize_from_partials(out, mm)
+    elif args.kernel == "attention":
+        from iconnx_b200.engine import GpuGraphExecutor
+        ex = GpuGraphExecutor.new(0)
+        out = graphs.build_bert(ex, graphs.BertConfig(layers=1, vocab=1000), M, K)
+        ex.set_cuda_graphs(False)
+        inp = graphs.bert_inputs(M, K, vocab=1000)
+        for _ in range(2):
+            ex.run(inp, [out])
+    torch.cuda.synchronize()
+    print(f"kernel probe {args.kernel} {args.shape} done", file=sys.stderr)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -425,7 +478,14 @@ def main():
     ap.add_argument("--workload", default="distilbert", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--kernel", choices=["ffn1", "gemm", "quant", "residual", "attention"],
+                    help="launch one kernel of the path a few times and exit (ncu captures)")
+    ap.add_argument("--shape", default="4096,768,3072",
+                    help="M,K,N for --kernel (attention: batch,seq,0)")
     args = ap.parse_args()
+    if args.kernel:
+        run_kernel_probe(args)
+        return
     args.warmup = max(args.warmup, 3)
 
     if args.impl == "reference":
@@ -528,7 +588,10 @@ def main():
     else:
         roof = {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                 "frac": gbs / peaks["hbm_gbs"], "peak_source": f"{peak_kind} hbm_gbs"}
-    roof.update({"traffic": None, "kernel": kdesc, "kernel_ms": k_ms, "int8_tops": tops,
+    traffic = roofline_traffic(kdesc)
+    roof.update({"traffic": traffic, "traffic_note": "ncu dram read+write bytes per launch (profiles/), "
+                 "scaled by rows where the capture used a smaller M", "algorithmic_bytes": bytes_alg,
+                 "kernel": kdesc, "kernel_ms": k_ms, "int8_tops": tops,
                  "tensor_frac_of_4500": tops / INT8_PEAK_TOPS})
 
     line = {"metric": METRIC, "value": value, "unit": wl.unit, "n_gpus": world,
