@@ -120,6 +120,10 @@ class BertConfig:
     per_channel: bool = False      # config 4: per-column w_scale and b_zp
     token_type: bool = False       # BERT adds a token-type embedding row
     eps: float = 1e-12
+    # per-tensor weight scale: int8 weights uniform over [-128, 127] times
+    # this give an effective weight std of ~0.04, the range of trained BERT
+    # Linears (attention scores of order 1-10, not 10^3)
+    w_scale: float = 0.0005
 
 
 DISTILBERT = BertConfig()
@@ -164,10 +168,10 @@ def build_bert(g, cfg: BertConfig, batch: int, seq: int) -> str:
         def lin(qz, K, N, seed, gelu=False):
             W = synth.int8_uniform((K, N), base + seed)
             if cfg.per_channel:
-                ws = synth.uniform_f32((N,), 0.005, 0.02, base + seed + 40)
+                ws = synth.uniform_f32((N,), 0.5 * cfg.w_scale, 2.0 * cfg.w_scale, base + seed + 40)
                 bz = synth.int8_uniform((N,), base + seed + 50, -8, 8)
             else:
-                ws, bz = np.array([0.01], np.float32), None
+                ws, bz = np.array([cfg.w_scale], np.float32), None
             return quant_linear(g, qz, nm, W, ws, synth.normal((N,), 0.02, base + seed + 20), bz, gelu)
 
         qx = dql(g, x, nm)
@@ -202,6 +206,61 @@ def build_bert(g, cfg: BertConfig, batch: int, seq: int) -> str:
         x = layernorm(g, r2, nm, H, base + 18, cfg.eps)
     g.add_node("output", "Identity", [x], ["last_hidden_state"])
     return "last_hidden_state"
+
+
+def build_attention(g, batch: int, seq: int, hidden: int = 768, heads: int = 12,
+                    mask: str = "batch") -> str:
+    """The encoder's self-attention block alone: graph inputs q, k, v
+    [batch, seq, hidden] f32 and, for mask "batch" / "shared", an additive
+    mask [batch, 1, 1, seq] / [1, 1, 1, seq]; Reshape / Transpose into heads,
+    MatMul, Div(sqrt(dh)), Add(mask), Softmax, MatMul, Transpose, Reshape.
+    Output "ctx" [batch, seq, hidden]."""
+    nm = _Namer()
+    dh = hidden // heads
+    for t in ("q", "k", "v"):
+        g.add_input(t, [batch, seq, hidden], np.float32)
+    if mask == "batch":
+        g.add_input("mask_bias", [batch, 1, 1, seq], np.float32)
+    elif mask == "shared":
+        g.add_input("mask_bias", [1, 1, 1, seq], np.float32)
+    g.add_initializer("shape_heads", np.array([0, 0, heads, dh], np.int64))
+    g.add_initializer("shape_hidden", np.array([0, 0, hidden], np.int64))
+    g.add_initializer("attn_div", np.array(np.sqrt(dh), np.float32))
+
+    def split(t, perm):
+        r, tr = nm("heads"), nm("heads_t")
+        g.add_node(nm("reshape"), "Reshape", [t, "shape_heads"], [r])
+        g.add_node(nm("transpose"), "Transpose", [r], [tr], {"perm": perm})
+        return tr
+
+    qh, kt, vh = split("q", [0, 2, 1, 3]), split("k", [0, 2, 3, 1]), split("v", [0, 2, 1, 3])
+    g.add_node("qk", "MatMul", [qh, kt], ["scores"])
+    g.add_node("div", "Div", ["scores", "attn_div"], ["scaled"])
+    sm_in = "scaled"
+    if mask in ("batch", "shared"):
+        g.add_node("add_mask", "Add", ["scaled", "mask_bias"], ["masked"])
+        sm_in = "masked"
+    g.add_node("softmax", "Softmax", [sm_in], ["probs"], {"axis": -1})
+    g.add_node("pv", "MatMul", ["probs", vh], ["ctx_h"])
+    g.add_node("ctx_t", "Transpose", ["ctx_h"], ["ctx_t"], {"perm": [0, 2, 1, 3]})
+    g.add_node("ctx_r", "Reshape", ["ctx_t", "shape_hidden"], ["ctx"])
+    return "ctx"
+
+
+def attention_reference(q, k, v, heads: int, mask_bias=None) -> np.ndarray:
+    """float64 evaluation of build_attention's graph (for tolerances)."""
+    B, S, H = q.shape
+    dh = H // heads
+
+    def split(t):
+        return t.astype(np.float64).reshape(B, S, heads, dh).transpose(0, 2, 1, 3)
+
+    s = split(q) @ split(k).transpose(0, 1, 3, 2) / np.float64(np.float32(np.sqrt(dh)))
+    if mask_bias is not None:
+        s = s + mask_bias.astype(np.float64)
+    s = np.exp(s - s.max(axis=-1, keepdims=True))
+    p = s / s.sum(axis=-1, keepdims=True)
+    return (p @ split(v)).transpose(0, 2, 1, 3).reshape(B, S, H)
 
 
 def layernorm(g, x: str, nm: _Namer, H: int, seed: int, eps: float) -> str:
