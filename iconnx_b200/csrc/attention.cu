@@ -353,7 +353,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   }
   // the first K / V tile into registers
   float4 nk[2], nv[2];
+  float nm = 0.0f;  // the tile's additive mask value for key tid (tid < 64)
   auto load_kv = [&](int k0) {
+    if (tid < kTcK) {
+      const int key = k0 + tid;
+      nm = key >= S ? -INFINITY : (mrow ? __ldg(mrow + key) : 0.0f);
+    }
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
       const int kr = k0 + kv_row + 32 * i;
@@ -394,10 +399,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       split_store(sm + kOffVh, sm + kOffVl, kKAtom, v_d, v_key + 4 * i, nv[i]);
     }
     // the tile's additive mask; keys past S get -inf
-    if (tid < kTcK) {
-      const int key = k0 + tid;
-      m_tile[tid] = key >= S ? -INFINITY : (mrow ? __ldg(mrow + key) : 0.0f);
-    }
+    if (tid < kTcK) m_tile[tid] = nm;
     fence_proxy_async_smem();
     tc_fence_before();
     ok = __syncthreads_and(ok) != 0;
@@ -429,16 +431,23 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
     for (int j = 0; j < kTcCols; ++j) p[j] = 0.0f;
     if (ok) {
-      // (((acc3 / 2^24 + acc2 / 2^16) + acc1 / 2^8) + acc0), one rounding per step
-      constexpr float kStep[4] = {1.0f, 0.00390625f, 1.52587890625e-05f, 5.9604644775390625e-08f};
+      // (((acc3 / 2^24 + acc2 / 2^16) + acc1 / 2^8) + acc0), one rounding per
+      // step; the four loads are in flight together
+      uint32_t r0[16], r1[16], r2[16], r3[16];
+      tmem_ld_32x32b_x16(t_row + (uint32_t)(3 * kTcK), r3);
+      tmem_ld_32x32b_x16(t_row + (uint32_t)(2 * kTcK), r2);
+      tmem_ld_32x32b_x16(t_row + (uint32_t)(1 * kTcK), r1);
+      tmem_ld_32x32b_x16(t_row, r0);
+      tmem_ld_wait_regs16(r3);
+      tmem_ld_wait_regs16(r2);
+      tmem_ld_wait_regs16(r1);
+      tmem_ld_wait_regs16(r0);
 #pragma unroll
-      for (int L = 3; L >= 0; --L) {
-        uint32_t r[16];
-        tmem_ld_32x32b_x16(t_row + (uint32_t)(L * kTcK), r);
-        tmem_ld_wait_regs16(r);
-#pragma unroll
-        for (int j = 0; j < kTcCols; ++j)
-          p[j] = __fmaf_rn((float)(int32_t)r[j], kStep[L], p[j]);
+      for (int j = 0; j < kTcCols; ++j) {
+        float f = __fmul_rn((float)(int32_t)r3[j], 5.9604644775390625e-08f);
+        f = __fmaf_rn((float)(int32_t)r2[j], 1.52587890625e-05f, f);
+        f = __fmaf_rn((float)(int32_t)r1[j], 0.00390625f, f);
+        p[j] = __fadd_rn((float)(int32_t)r0[j], f);
       }
     }
     // scale by 2^(nq + nk), Div(c), Add(mask) (-inf past S)
