@@ -206,41 +206,52 @@ __global__ void __launch_bounds__(kAttThreads)
 // hi*hi + hi*lo + lo*hi (three kind::tf32 MMAs); errors there are not
 // amplified (p <= 1).
 //
-// 16 warps: query row r is TMEM lane r; warp w reads lanes 32*(w%4) .. +31
-// (the quadrant a warp may access) and owns columns 16*(w/4) .. +15 of every
-// 64-key tile, so four warps share a row and exchange its running max / sum
-// through shared memory.  Per 64-key tile:
-//   1. all threads slice the tile's K rows (bytes, [key][slice pair][d]) and
-//      split V (tf32 hi / lo, stored transposed as [d][key]), both in the
-//      128-byte-swizzled K-major layout the MMA reads; the registers were
-//      loaded while the previous tile was processed;
-//   2. thread 0 issues the 20 integer MMAs of S (M=128, N=64, K=32) into
-//      TMEM columns [64 L, 64 L + 64) for L = 0..3;
-//   3. each thread combines its 16 scores, applies Div(c) and Add(mask); the
-//      row max over the four warps gives the online-softmax update; the
-//      unnormalised probabilities P go, split, to shared memory;
-//   4. thread 0 issues O_tile = P V (M=128, N=64, K=64 keys) into columns
-//      [256, 320); each thread rescales its 16 accumulator columns and adds
-//      its O_tile slice.
+// 8 warps, two CTAs per SM (84 KB shared memory, 256 TMEM columns each), so
+// one CTA's MMA waits and load latencies overlap the other's work.  Query
+// row r is TMEM lane r; warp w reads lanes 32*(w%4) .. +31 (the quadrant a
+// warp may access) and owns columns 32*(w/4) .. +31 of every 64-key tile and
+// of the context, so two warps share a row and exchange its running max /
+// sum through shared memory.  Per 64-key tile:
+//   1. all threads slice the tile's K rows (bytes, [key][slice pair][d],
+//      loaded into registers during the previous tile) into the
+//      128-byte-swizzled K-major layout the MMA reads;
+//   2. thread 0 issues the 20 integer MMAs of S (M=128, N=64, K=32) into TMEM
+//      columns [64 L, 64 L + 64) for L = 0..3; meanwhile all threads load V,
+//      split it into tf32 hi / lo and store it transposed ([d][key]);
+//   3. each thread combines its 32 scores, applies Div(c) and Add(mask); the
+//      row max over the two warps gives the online-softmax update; the
+//      unnormalised probabilities P, split hi / lo, are written back into
+//      TMEM columns [0,64) / [64,128) (the consumed score columns);
+//   4. thread 0 issues O_tile = P V (M=128, N=64, K=64 keys; A = P read from
+//      TMEM, B = V^T from shared memory) into columns [128,192); meanwhile
+//      all threads load the next K tile; each thread rescales its 32
+//      accumulator columns and adds its O_tile slice.
 constexpr int kTcQ = 128;
 constexpr int kTcK = 64;
-constexpr int kTcThreads = 512;
-constexpr int kTcCols = 16;           // score / context columns per thread
+constexpr int kTcThreads = 256;
+constexpr int kTcCols = 32;           // score / context columns per thread
 constexpr int kQAtom = kTcQ * 128;    // one 128-byte-wide column block of 128 rows
 constexpr int kKAtom = kTcK * 128;    // one 128-byte-wide column block of 64 rows
 constexpr int kOffQs = 0;                              // Q slices: 2 blocks (slices 0|1, 2|3)
 constexpr int kOffKs = kOffQs + 2 * kQAtom;            // K slices: 2 blocks
 constexpr int kOffVh = kOffKs + 2 * kKAtom;            // V^T hi / lo: 2 blocks each
 constexpr int kOffVl = kOffVh + 2 * kKAtom;
-constexpr int kOffPh = kOffVl + 2 * kKAtom;            // P hi / lo: 2 blocks each
-constexpr int kOffPl = kOffPh + 2 * kQAtom;
-constexpr int kOffRed = kOffPl + 2 * kQAtom;           // [4][128] partial max, [4][128] partial sum
-constexpr int kOffScale = kOffRed + 2 * 4 * kTcQ * 4;  // 2^nq per query row, 2^nk per key
+constexpr int kOffRed = kOffVl + 2 * kKAtom;           // [2][128] partial max, [2][128] partial sum
+constexpr int kOffScale = kOffRed + 2 * 2 * kTcQ * 4;  // 2^(nq-1) per query row, 2^(nk-1) per key
 constexpr int kOffMask = kOffScale + (kTcQ + kTcK) * 4;  // additive mask per key of the tile
 constexpr int kOffBar = kOffMask + kTcK * 4;
 constexpr int kTcSmem = kOffBar + 64 + 1024 /*align slack*/;
-constexpr uint32_t kTcTmemCols = 512;
-constexpr int kTmemO = 4 * kTcK;  // O_tile columns
+constexpr uint32_t kTcTmemCols = 256;
+constexpr int kTmemPh = 0;        // P hi (after the scores are consumed)
+constexpr int kTmemPl = kTcK;     // P lo
+constexpr int kTmemO = 2 * kTcK;  // O_tile
+static_assert(2 * kTcSmem <= 227 * 1024, "two CTAs per SM");
+
+// The value of x, hidden from the optimiser (no hoisting of what depends on it).
+__device__ __forceinline__ uint32_t opaque_u32(uint32_t x) {
+  asm volatile("mov.b32 %0, %0;" : "+r"(x));
+  return x;
+}
 
 // Round to the nearest TF32 value (ties away from zero) by integer
 // arithmetic on the bit pattern.
@@ -302,7 +313,8 @@ __device__ __forceinline__ float slice_row_store(uint8_t* base, int block, int r
   return pow2f(n - 1);
 }
 
-__global__ void __launch_bounds__(kTcThreads, 1)
+template <bool C_POW2>
+__global__ void __launch_bounds__(kTcThreads, 2)
     attention_tc_kernel(const float* __restrict__ q, const float* __restrict__ k,
                         const float* __restrict__ v, int ld, float* __restrict__ out, int H, int S,
                         int nh, float c, const float* __restrict__ mask, int mask_per_batch) {
@@ -310,7 +322,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint8_t* sm = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(att_raw) + 1023) & ~uintptr_t(1023));
   float* red_max = reinterpret_cast<float*>(sm + kOffRed);
-  float* red_sum = red_max + 4 * kTcQ;
+  float* red_sum = red_max + 2 * kTcQ;
   float* q_scale = reinterpret_cast<float*>(sm + kOffScale);
   float* k_scale = q_scale + kTcQ;
   float* m_tile = reinterpret_cast<float*>(sm + kOffMask);
@@ -326,13 +338,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int q0 = blockIdx.x * kTcQ;
   const size_t head = (size_t)b * S * ld + (size_t)h * kAttDh;
   const float* mrow = mask ? mask + (mask_per_batch ? (size_t)b * S : 0) : nullptr;
-  int cexp;
-  const bool c_pow2 = frexpf(c, &cexp) == 0.5f;
-  const float inv_c = 1.0f / c;
+  const float inv_c = 1.0f / c;  // exact when c is a power of two (C_POW2)
   // Q / K rows: 16 threads per 256-byte row; V: thread = column d (tid % 64)
-  // of keys 8 (tid / 64) .. +7, stored as row d of V^T
+  // of keys 16 (tid / 64) .. +15, stored as row d of V^T
   const int kv_row = tid >> 4, kv_col = (tid & 15) * 4;
-  const int v_d = tid & 63, v_key = (tid >> 6) * 8;
+  const int v_d = tid & 63, v_key = (tid >> 6) * 16;
 
   if (tid == 0) {
     mbar_init(bar_s, 1);
@@ -343,46 +353,43 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     tmem_alloc(tslot, kTcTmemCols);
     tmem_relinquish();
   }
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int r = (i * kTcThreads + tid) >> 4, qi = q0 + r;
-    const float4 x = qi < S ? __ldg(reinterpret_cast<const float4*>(q + head + (size_t)qi * ld + kv_col))
-                            : make_float4(0.f, 0.f, 0.f, 0.f);
-    const float f = slice_row_store(sm + kOffQs, kQAtom, r, kv_col, x);
-    if (kv_col == 0) q_scale[r] = f;
-  }
-  // the first K / V tile into registers
-  float4 nk[2], nv[2];
+  float4 nk[4];
   float nm = 0.0f;  // the tile's additive mask value for key tid (tid < 64)
-  auto load_kv = [&](int k0) {
+  auto load_k = [&](int k0) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int kr = k0 + kv_row + 16 * i;
+      nk[i] = kr < S ? __ldg(reinterpret_cast<const float4*>(k + head + (size_t)kr * ld + kv_col))
+                     : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
     if (tid < kTcK) {
       const int key = k0 + tid;
       nm = key >= S ? -INFINITY : (mrow ? __ldg(mrow + key) : 0.0f);
     }
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      const int kr = k0 + kv_row + 32 * i;
-      nk[i] = kr < S ? __ldg(reinterpret_cast<const float4*>(k + head + (size_t)kr * ld + kv_col))
-                     : make_float4(0.f, 0.f, 0.f, 0.f);
-      float x[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int vr = k0 + v_key + 4 * i + u;
-        x[u] = vr < S ? __ldg(v + head + (size_t)vr * ld + v_d) : 0.0f;
-      }
-      nv[i] = make_float4(x[0], x[1], x[2], x[3]);
-    }
   };
-  load_kv(0);
+  {
+    float4 vq[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int r = (i * kTcThreads + tid) >> 4, qi = q0 + r;
+      vq[i] = qi < S ? __ldg(reinterpret_cast<const float4*>(q + head + (size_t)qi * ld + kv_col))
+                     : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    load_k(0);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int r = (i * kTcThreads + tid) >> 4;
+      const float f = slice_row_store(sm + kOffQs, kQAtom, r, kv_col, vq[i]);
+      if (kv_col == 0) q_scale[r] = f;
+    }
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tslot;
-  const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)col0;
+  const uint32_t t_lane = tmem_base + ((uint32_t)(quad * 32) << 16);  // this warp's lanes
   constexpr uint32_t idesc_o = idesc_tf32(kTcQ, kAttDh, false);
-  const uint32_t a_qs = smem_addr(sm + kOffQs), a_ks = smem_addr(sm + kOffKs);
-  const uint32_t a_v_h = smem_addr(sm + kOffVh), a_v_l = smem_addr(sm + kOffVl);
-  const uint32_t a_p_h = smem_addr(sm + kOffPh), a_p_l = smem_addr(sm + kOffPl);
+  const uint32_t a_sm = smem_addr(sm);
   const float qsc = q_scale[row];
   const float qf = __fmul_rn(qsc, inv_c);  // a power of two when c is
 
@@ -392,20 +399,23 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   bool ok = true;
   uint32_t phase = 0;
   for (int k0 = 0; k0 < S; k0 += kTcK, phase ^= 1) {
+    // 1. K slices and the mask of this tile
 #pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      const float f = slice_row_store(sm + kOffKs, kKAtom, kv_row + 32 * i, kv_col, nk[i]);
-      if (kv_col == 0) k_scale[kv_row + 32 * i] = f;
-      split_store(sm + kOffVh, sm + kOffVl, kKAtom, v_d, v_key + 4 * i, nv[i]);
+    for (int i = 0; i < 4; ++i) {
+      const float f = slice_row_store(sm + kOffKs, kKAtom, kv_row + 16 * i, kv_col, nk[i]);
+      if (kv_col == 0) k_scale[kv_row + 16 * i] = f;
     }
-    // the tile's additive mask; keys past S get -inf
     if (tid < kTcK) m_tile[tid] = nm;
     fence_proxy_async_smem();
     tc_fence_before();
     ok = __syncthreads_and(ok) != 0;
     if (!ok) break;
+    // 2. S = Q K^T, exact per level; V^T of this tile meanwhile
     if (tid == 0) {
       tc_fence_after();
+      // the operand addresses are made opaque here so the compiler does not
+      // hoist 40 loop-invariant descriptors into registers for the whole loop
+      const uint32_t a_qs = opaque_u32(a_sm + kOffQs), a_ks = opaque_u32(a_sm + kOffKs);
 #pragma unroll
       for (int L = 0; L < 4; ++L) {
 #pragma unroll
@@ -413,10 +423,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           const int j = L - i;
 #pragma unroll
           for (int hd = 0; hd < 2; ++hd) {
-            // slice i of Q / slice j of K, d half hd (32 bytes each)
+            // slice i of Q / slice j of K, d half hd (32 bytes each); the
+            // most significant slice is signed, the others unsigned
             const uint32_t ao = (i >> 1) * kQAtom + (i & 1) * 64 + hd * 32;
             const uint32_t bo = (j >> 1) * kKAtom + (j & 1) * 64 + hd * 32;
-            // the most significant slice is signed, the others unsigned
             mma_i8(tmem_base + (uint32_t)(L * kTcK), smem_desc_k128(a_qs + ao),
                    smem_desc_k128(a_ks + bo), idesc_i8(kTcQ, kTcK, i == 0, j == 0), (i | hd) != 0);
           }
@@ -424,92 +434,126 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
       mma_commit(bar_s);
     }
-    if (k0 + kTcK < S) load_kv(k0 + kTcK);  // lands while this tile is processed
+    {
+      float4 nv[4];
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        float x[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int vr = k0 + v_key + 4 * g + u;
+          x[u] = vr < S ? __ldg(v + head + (size_t)vr * ld + v_d) : 0.0f;
+        }
+        nv[g] = make_float4(x[0], x[1], x[2], x[3]);
+      }
+#pragma unroll
+      for (int g = 0; g < 4; ++g)
+        split_store(sm + kOffVh, sm + kOffVl, kKAtom, v_d, v_key + 4 * g, nv[g]);
+    }
     ok = mbar_wait_warp(bar_s, phase, ICX_DEVICE_TIMEOUT_EPILOGUE);
     tc_fence_after();
-    float p[kTcCols];
-#pragma unroll
-    for (int j = 0; j < kTcCols; ++j) p[j] = 0.0f;
-    if (ok) {
-      // (((acc3 / 2^24 + acc2 / 2^16) + acc1 / 2^8) + acc0), one rounding per
-      // step; the four loads are in flight together
-      uint32_t r0[16], r1[16], r2[16], r3[16];
-      tmem_ld_32x32b_x16(t_row + (uint32_t)(3 * kTcK), r3);
-      tmem_ld_32x32b_x16(t_row + (uint32_t)(2 * kTcK), r2);
-      tmem_ld_32x32b_x16(t_row + (uint32_t)(1 * kTcK), r1);
-      tmem_ld_32x32b_x16(t_row, r0);
-      tmem_ld_wait_regs16(r3);
-      tmem_ld_wait_regs16(r2);
-      tmem_ld_wait_regs16(r1);
-      tmem_ld_wait_regs16(r0);
-#pragma unroll
-      for (int j = 0; j < kTcCols; ++j) {
-        float f = __fmul_rn((float)(int32_t)r3[j], 5.9604644775390625e-08f);
-        f = __fmaf_rn((float)(int32_t)r2[j], 1.52587890625e-05f, f);
-        f = __fmaf_rn((float)(int32_t)r1[j], 0.00390625f, f);
-        p[j] = __fadd_rn((float)(int32_t)r0[j], f);
-      }
-    }
-    // scale by 2^(nq + nk), Div(c), Add(mask) (-inf past S)
+    // 3. scores: (((acc3 / 2^24 + acc2 / 2^16) + acc1 / 2^8) + acc0), one
+    // rounding per step, then 2^(nq-1) 2^(nk-1), Div(c), Add(mask)
     float pmax = -INFINITY;
 #pragma unroll
-    for (int j = 0; j < kTcCols; ++j) {
-      float t;
-      if (c_pow2) {
-        t = __fmul_rn(__fmul_rn(p[j], qf), k_scale[col0 + j]);  // exact: powers of two
-      } else {
-        t = __fdiv_rn(__fmul_rn(__fmul_rn(p[j], qsc), k_scale[col0 + j]), c);
+    for (int hcol = 0; hcol < kTcCols; hcol += 16) {
+      const uint32_t t = t_lane + (uint32_t)(col0 + hcol);
+      float f[16];
+      uint32_t sc[16];
+      // one level at a time (16 registers in flight)
+#pragma unroll
+      for (int L = 3; L >= 0; --L) {
+        uint32_t r[16];
+        if (ok) {
+          tmem_ld_32x32b_x16(t + (uint32_t)(L * kTcK), r);
+          tmem_ld_wait_regs16(r);
+        }
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const float a = (float)(int32_t)r[j];
+          f[j] = L == 3 ? __fmul_rn(a, 5.9604644775390625e-08f)
+               : L == 2 ? __fmaf_rn(a, 1.52587890625e-05f, f[j])
+               : L == 1 ? __fmaf_rn(a, 0.00390625f, f[j])
+                        : __fadd_rn(a, f[j]);
+        }
       }
-      t = __fadd_rn(t, m_tile[col0 + j]);
-      p[j] = t;
-      pmax = fmaxf(pmax, t);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const float g = f[j];
+        const int jj = col0 + hcol + j;
+        float t2 = C_POW2 ? __fmul_rn(__fmul_rn(g, qf), k_scale[jj])  // exact: powers of two
+                          : __fdiv_rn(__fmul_rn(__fmul_rn(g, qsc), k_scale[jj]), c);
+        t2 = __fadd_rn(t2, m_tile[jj]);  // -inf past S
+        sc[j] = __float_as_uint(t2);
+        pmax = fmaxf(pmax, t2);
+      }
+      // park the scores in their (consumed) level-0 columns until the row max
+      // is known
+      tmem_st_32x32b_x16(t, sc);
     }
+    tmem_st_wait();
     red_max[cg * kTcQ + row] = pmax;
-    ok = __syncthreads_and(ok) != 0;
+    tc_fence_before();
+    ok = __syncthreads_and(ok) != 0;  // every score column has been read
     if (!ok) break;
-    const float tmax = fmaxf(fmaxf(red_max[row], red_max[kTcQ + row]),
-                             fmaxf(red_max[2 * kTcQ + row], red_max[3 * kTcQ + row]));
+    tc_fence_after();
+    const float tmax = fmaxf(red_max[row], red_max[kTcQ + row]);
     // online softmax: exp(a - m) = 2^(a*log2e - m*log2e)
     const float m_new = fmaxf(m_run, tmax);
     const float ml = m_new == -INFINITY ? 0.0f : m_new * kLog2e;  // a fully masked row stays 0
     const float alpha = m_run == -INFINITY ? 0.0f : ex2f(fmaf(m_run, kLog2e, -ml));
     float rsum = 0.0f;
 #pragma unroll
-    for (int j = 0; j < kTcCols; ++j) {
-      p[j] = ex2f(fmaf(p[j], kLog2e, -ml));  // 2^-inf = 0 for masked keys
-      rsum += p[j];
+    for (int hcol = 0; hcol < kTcCols; hcol += 16) {
+      uint32_t hi[16], lo[16], sc[16];
+      tmem_ld_32x32b_x16(t_lane + (uint32_t)(col0 + hcol), sc);
+      tmem_ld_wait_regs16(sc);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const float e = ex2f(fmaf(__uint_as_float(sc[j]), kLog2e, -ml));  // 2^-inf = 0 for masked keys
+        rsum += e;
+        const float eh = tf32_round(e);
+        hi[j] = __float_as_uint(eh);
+        lo[j] = __float_as_uint(tf32_round(__fsub_rn(e, eh)));
+      }
+      tmem_st_32x32b_x16(t_lane + (uint32_t)(kTmemPh + col0 + hcol), hi);
+      tmem_st_32x32b_x16(t_lane + (uint32_t)(kTmemPl + col0 + hcol), lo);
     }
     l_part = l_part * alpha + rsum;
     m_run = m_new;
-#pragma unroll
-    for (int j = 0; j < kTcCols; j += 4)
-      split_store(sm + kOffPh, sm + kOffPl, kQAtom, row, col0 + j,
-                  make_float4(p[j], p[j + 1], p[j + 2], p[j + 3]));
-    fence_proxy_async_smem();
+    tmem_st_wait();
+    fence_proxy_async_smem();  // V^T stores -> the MMA
     tc_fence_before();
     __syncthreads();
+    // 4. O_tile = P V; the next K tile meanwhile
     if (tid == 0) {
       tc_fence_after();
+      const uint32_t a_v_h = opaque_u32(a_sm + kOffVh), a_v_l = opaque_u32(a_sm + kOffVl);
 #pragma unroll
       for (int j = 0; j < kTcK / 8; ++j) {
-        // k-step j = keys 8j..8j+7: P column block j/4, V^T column block j/4
-        const uint32_t ao = (j >> 2) * kQAtom + (j & 3) * 32, bo = (j >> 2) * kKAtom + (j & 3) * 32;
-        const uint64_t ph = smem_desc_k128(a_p_h + ao), pl = smem_desc_k128(a_p_l + ao);
+        // k-step j = keys 8j..8j+7: P columns 8j.., V^T column block j/4
+        const uint32_t bo = (j >> 2) * kKAtom + (j & 3) * 32;
         const uint64_t vh = smem_desc_k128(a_v_h + bo), vl = smem_desc_k128(a_v_l + bo);
-        mma_tf32(tmem_base + kTmemO, ph, vh, idesc_o, j > 0);
-        mma_tf32(tmem_base + kTmemO, ph, vl, idesc_o, true);
-        mma_tf32(tmem_base + kTmemO, pl, vh, idesc_o, true);
+        const uint32_t ph = tmem_base + (uint32_t)(kTmemPh + 8 * j);
+        const uint32_t pl = tmem_base + (uint32_t)(kTmemPl + 8 * j);
+        mma_tf32_ts(tmem_base + kTmemO, ph, vh, idesc_o, j > 0);
+        mma_tf32_ts(tmem_base + kTmemO, ph, vl, idesc_o, true);
+        mma_tf32_ts(tmem_base + kTmemO, pl, vh, idesc_o, true);
       }
       mma_commit(bar_o);
     }
+    if (k0 + kTcK < S) load_k(k0 + kTcK);
     ok = mbar_wait_warp(bar_o, phase, ICX_DEVICE_TIMEOUT_EPILOGUE);
     tc_fence_after();
     if (ok) {
-      uint32_t r[16];
-      tmem_ld_32x32b_x16(t_row + kTmemO, r);
-      tmem_ld_wait_regs16(r);
 #pragma unroll
-      for (int d = 0; d < kTcCols; ++d) o[d] = fmaf(o[d], alpha, __uint_as_float(r[d]));
+      for (int hcol = 0; hcol < kTcCols; hcol += 16) {
+        uint32_t r[16];
+        tmem_ld_32x32b_x16(t_lane + (uint32_t)(kTmemO + col0 + hcol), r);
+        tmem_ld_wait_regs16(r);
+#pragma unroll
+        for (int d = 0; d < 16; ++d) o[hcol + d] = fmaf(o[hcol + d], alpha, __uint_as_float(r[d]));
+      }
     }
     // TMEM reads of this tile are done before the next tile's MMAs overwrite
     tc_fence_before();
@@ -518,8 +562,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   ok = __syncthreads_and(ok) != 0;
   const int qi = q0 + row;
   if (ok && qi < S) {
-    const float l = (red_sum[row] + red_sum[kTcQ + row]) + (red_sum[2 * kTcQ + row] + red_sum[3 * kTcQ + row]);
-    const float inv = 1.0f / l;
+    const float inv = 1.0f / (red_sum[row] + red_sum[kTcQ + row]);
     float4* orow = reinterpret_cast<float4*>(out + ((size_t)b * S + qi) * H + (size_t)h * kAttDh + col0);
 #pragma unroll
     for (int d = 0; d < kTcCols; d += 4)
@@ -551,11 +594,13 @@ int launch_attention_f32(cudaStream_t s, const float* q, const float* k, const f
   }();
   if (!simt) {
     ICX_REQUIRE(B * nh <= 65535, "Attention: batch x heads %lld too large", (long long)(B * nh));
-    ICX_CUDA(cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  kTcSmem));
+    int cexp;
+    const bool c_pow2 = frexpf(c, &cexp) == 0.5f;
+    auto kern = c_pow2 ? attention_tc_kernel<true> : attention_tc_kernel<false>;
+    ICX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem));
     dim3 grid((unsigned)((S + kTcQ - 1) / kTcQ), (unsigned)(B * nh));
-    attention_tc_kernel<<<grid, kTcThreads, kTcSmem, s>>>(q, k, v, (int)ld, out, (int)H, (int)S,
-                                                            (int)nh, c, mask, mask_per_batch ? 1 : 0);
+    kern<<<grid, kTcThreads, kTcSmem, s>>>(q, k, v, (int)ld, out, (int)H, (int)S, (int)nh, c, mask,
+                                           mask_per_batch ? 1 : 0);
     ICX_LAUNCH_CHECK();
     return ICX_OK;
   }
