@@ -317,7 +317,8 @@ template <bool C_POW2>
 __global__ void __launch_bounds__(kTcThreads, 2)
     attention_tc_kernel(const float* __restrict__ q, const float* __restrict__ k,
                         const float* __restrict__ v, int ld, float* __restrict__ out, int H, int S,
-                        int nh, float c, const float* __restrict__ mask, int mask_per_batch) {
+                        int nh, float c, const float* __restrict__ mask, int mask_per_batch,
+                        float2* __restrict__ minmax) {
   extern __shared__ __align__(1024) uint8_t att_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(att_raw) + 1023) & ~uintptr_t(1023));
@@ -561,12 +562,37 @@ __global__ void __launch_bounds__(kTcThreads, 2)
   red_sum[cg * kTcQ + row] = l_part;
   ok = __syncthreads_and(ok) != 0;
   const int qi = q0 + row;
+  float mn = 0.0f, mx = 0.0f;  // (min, max) of what this CTA writes, seeded like DynamicQuantizeLinear
   if (ok && qi < S) {
     const float inv = 1.0f / (red_sum[row] + red_sum[kTcQ + row]);
     float4* orow = reinterpret_cast<float4*>(out + ((size_t)b * S + qi) * H + (size_t)h * kAttDh + col0);
 #pragma unroll
-    for (int d = 0; d < kTcCols; d += 4)
-      orow[d / 4] = make_float4(o[d] * inv, o[d + 1] * inv, o[d + 2] * inv, o[d + 3] * inv);
+    for (int d = 0; d < kTcCols; d += 4) {
+      const float4 w = make_float4(o[d] * inv, o[d + 1] * inv, o[d + 2] * inv, o[d + 3] * inv);
+      orow[d / 4] = w;
+      mn = fminf(fminf(mn, fminf(w.x, w.y)), fminf(w.z, w.w));
+      mx = fmaxf(fmaxf(mx, fmaxf(w.x, w.y)), fmaxf(w.z, w.w));
+    }
+  }
+  if (minmax != nullptr) {
+    // one partial per CTA for the DynamicQuantizeLinear that reads `out`
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, off));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    }
+    if (lane == 0) {
+      red_max[warp] = mn;  // the row max / sum areas are free now
+      red_max[8 + warp] = mx;
+    }
+    __syncthreads();
+    if (tid == 0) {
+      for (int w = 1; w < kTcThreads / 32; ++w) {
+        mn = fminf(mn, red_max[w]);
+        mx = fmaxf(mx, red_max[8 + w]);
+      }
+      minmax[blockIdx.y * gridDim.x + blockIdx.x] = make_float2(mn, mx);
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -580,28 +606,39 @@ bool attention_supported(int64_t dh, int64_t ld, int64_t H) {
   return dh == kAttDh && ld % 4 == 0 && H % 4 == 0;
 }
 
+int attention_partials(int64_t B, int64_t S, int64_t nh) {
+  return (int)(((S + kTcQ - 1) / kTcQ) * B * nh);
+}
+
 int launch_attention_f32(cudaStream_t s, const float* q, const float* k, const float* v, int64_t ld,
                          float* out, int64_t B, int64_t S, int64_t H, int64_t nh, float c,
-                         const float* mask, bool mask_per_batch) {
+                         const float* mask, bool mask_per_batch, float* minmax, int* n_minmax) {
   ICX_REQUIRE(attention_supported(H / nh, ld, H), "Attention: head size %lld unsupported",
               (long long)(H / nh));
   ICX_REQUIRE((((uintptr_t)q | (uintptr_t)k | (uintptr_t)v | (uintptr_t)out) & 15) == 0,
               "Attention: q/k/v/out must be 16-byte aligned");
-  if (B == 0 || S == 0 || nh == 0) return ICX_OK;
+  if (B == 0 || S == 0 || nh == 0) {
+    if (n_minmax) *n_minmax = 0;
+    return ICX_OK;
+  }
   static const bool simt = [] {
     const char* e = getenv("ICONNX_ATTENTION");
     return e != nullptr && strcmp(e, "simt") == 0;
   }();
   if (!simt) {
     ICX_REQUIRE(B * nh <= 65535, "Attention: batch x heads %lld too large", (long long)(B * nh));
+    const int parts = attention_partials(B, S, nh);
+    ICX_REQUIRE(minmax == nullptr || parts <= ICX_MAX_MINMAX_PARTIALS,
+                "Attention: %d (min, max) partials exceed %d", parts, ICX_MAX_MINMAX_PARTIALS);
     int cexp;
     const bool c_pow2 = frexpf(c, &cexp) == 0.5f;
     auto kern = c_pow2 ? attention_tc_kernel<true> : attention_tc_kernel<false>;
     ICX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem));
     dim3 grid((unsigned)((S + kTcQ - 1) / kTcQ), (unsigned)(B * nh));
     kern<<<grid, kTcThreads, kTcSmem, s>>>(q, k, v, (int)ld, out, (int)H, (int)S, (int)nh, c, mask,
-                                           mask_per_batch ? 1 : 0);
+                                           mask_per_batch ? 1 : 0, reinterpret_cast<float2*>(minmax));
     ICX_LAUNCH_CHECK();
+    if (n_minmax) *n_minmax = parts;
     return ICX_OK;
   }
   const int smem = 4 * kAttTile * kAttPad * (int)sizeof(float);
@@ -610,6 +647,13 @@ int launch_attention_f32(cudaStream_t s, const float* q, const float* k, const f
   attention_f32_kernel<<<grid, kAttThreads, smem, s>>>(q, k, v, (int)ld, out, (int)H, (int)S, (int)nh,
                                                        c, mask, mask_per_batch ? 1 : 0);
   ICX_LAUNCH_CHECK();
+  if (minmax != nullptr) {
+    // the CUDA-core kernel has no fused (min, max): one separate pass
+    const size_t n = (size_t)(B * S * H);
+    const int rc = launch_dql_minmax(s, out, n, reinterpret_cast<float2*>(minmax));
+    if (rc) return rc;
+    if (n_minmax) *n_minmax = dql_minmax_partials(n);
+  }
   return ICX_OK;
 }
 

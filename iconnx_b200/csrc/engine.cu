@@ -873,6 +873,12 @@ class Engine {
       bool ok = p.op == "LayerNormalization";
       for (auto& kv : fused_)
         if (kv.second.out == d.in[0]) ok = true;
+      for (auto& kv : attn_) {
+        const FusedAttn& a = kv.second;
+        if (a.out == d.in[0] && attention_supported(a.dh, a.ld ? a.ld : a.H, a.H) &&
+            attention_partials(a.B, a.S, a.nh) <= ICX_MAX_MINMAX_PARTIALS)
+          ok = true;
+      }
       if (!ok) continue;
       x.minmax_slot = slot;
       dql_mode_[idx] = slot;
@@ -1295,9 +1301,12 @@ class Engine {
       const float* mask = a.mask.empty() ? nullptr : static_cast<const float*>(resolve(a.mask));
       const FusedAttn at = a;
       const int64_t ld = a.ld ? a.ld : a.H;
+      const int slot = vals_[a.out].minmax_slot;
+      float* mm = slot >= 0 ? slot_ptr(slot) : nullptr;
+      int* mmc = slot >= 0 ? &minmax_count_[slot] : nullptr;
       add_step(n, "Attention", a.out, [=](cudaStream_t s) {
         return launch_attention_f32(s, q, k, v, ld, out, at.B, at.S, at.H, at.nh, at.c, mask,
-                                    at.mask_per_batch);
+                                    at.mask_per_batch, mm, mmc);
       }, 1);
       return ICX_OK;
     }
