@@ -57,3 +57,35 @@ def test_config4_linear_per_column_full_rows():
     x = synth.normal((M, K), 1.0, 6)
     _sampled_rows_check(x, synth.int8_uniform((K, N), 7), synth.uniform_f32((N,), 0.005, 0.02, 8),
                         synth.normal((N,), 0.02, 9), bz=synth.int8_uniform((N,), 10, -8, 8))
+
+
+@pytest.mark.parametrize("M,K,N,gelu", [
+    (4096, 768, 3072, True),    # config 3 FFN1 (GELU epilogue)
+    (4096, 768, 2304, False),   # config 3 merged Q/K/V
+    (4261, 768, 3000, True),    # ragged M and N: the last tiles read past M / N
+])
+def test_wide_shallow_gemm_sampled(M, K, N, gelu):
+    """Config 3's wide, shallow-K GEMMs at full size (and a ragged variant
+    whose last tiles run past M and N): every u8 of the quantised input and a
+    sample of output rows that includes the first and last ones, bit-exact
+    (1e-5 after GELU)."""
+    x = synth.normal((M, K), 1.0, 11)
+    w = synth.int8_uniform((K, N), 12)
+    ws = np.array([0.01], np.float32)
+    bias = synth.normal((N,), 0.02, 13)
+    pw = ops.prepare_weight(torch.from_numpy(w).to(DEV))
+    out, y, s, z = ops.dynamic_quant_linear(torch.from_numpy(x).to(DEV), pw,
+                                            torch.from_numpy(ws).to(DEV),
+                                            torch.from_numpy(bias).to(DEV), None, gelu=gelu)
+    oy, os_, oz = oracle.dynamic_quantize_linear(x)
+    np.testing.assert_array_equal(y.cpu().numpy(), oy)
+    rng = np.random.default_rng(14)
+    pick = np.unique(np.concatenate([rng.choice(M, 40, replace=False), np.arange(M - 8, M),
+                                     np.arange(0, 8), np.arange(128, 136), np.arange(256, 260)]))
+    acc = oracle.matmul_integer(oy[pick], w, np.uint8(oz), None, threads=8)
+    ref = (oracle.cast_i32_f32(acc) * (np.float32(os_) * ws[0]) + bias).astype(np.float32)
+    got = out[torch.from_numpy(pick).to(DEV)].cpu().numpy()
+    if gelu:
+        np.testing.assert_allclose(got, oracle.gelu(ref), rtol=0, atol=1e-5)
+    else:
+        np.testing.assert_array_equal(got.view(np.uint32), ref.view(np.uint32))
