@@ -44,6 +44,8 @@ __global__ void __launch_bounds__(kAttThreads)
                          const float* __restrict__ v, int ld, float* __restrict__ out,
                          int H, int S, int nh, float c, const float* __restrict__ mask,
                          int mask_per_batch) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ float sm[];
   float* sQ = sm;                           // [64][68] query rows
   float* sK = sQ + kAttTile * kAttPad;      // [64][68] key rows
@@ -354,6 +356,10 @@ __global__ void __launch_bounds__(kTcThreads, 2)
     tmem_alloc(tslot, kTcTmemCols);
     tmem_relinquish();
   }
+  // barrier init and TMEM allocation overlap the previous kernel; q / k / v
+  // (its outputs) are read only from here on
+  pdl_wait();
+  pdl_trigger();
   float4 nk[4];
   float nm = 0.0f;  // the tile's additive mask value for key tid (tid < 64)
   auto load_k = [&](int k0) {
@@ -635,7 +641,7 @@ int launch_attention_f32(cudaStream_t s, const float* q, const float* k, const f
     auto kern = c_pow2 ? attention_tc_kernel<true> : attention_tc_kernel<false>;
     ICX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem));
     dim3 grid((unsigned)((S + kTcQ - 1) / kTcQ), (unsigned)(B * nh));
-    kern<<<grid, kTcThreads, kTcSmem, s>>>(q, k, v, (int)ld, out, (int)H, (int)S, (int)nh, c, mask,
+    launch_pdl(kern, dim3(grid), dim3(kTcThreads), kTcSmem, s, q, k, v, (int)ld, out, (int)H, (int)S, (int)nh, c, mask,
                                            mask_per_batch ? 1 : 0, reinterpret_cast<float2*>(minmax));
     ICX_LAUNCH_CHECK();
     if (n_minmax) *n_minmax = parts;
@@ -644,7 +650,7 @@ int launch_attention_f32(cudaStream_t s, const float* q, const float* k, const f
   const int smem = 4 * kAttTile * kAttPad * (int)sizeof(float);
   ICX_CUDA(cudaFuncSetAttribute(attention_f32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
   dim3 grid((unsigned)(B * nh), (unsigned)((S + kAttTile - 1) / kAttTile));
-  attention_f32_kernel<<<grid, kAttThreads, smem, s>>>(q, k, v, (int)ld, out, (int)H, (int)S, (int)nh,
+  launch_pdl(attention_f32_kernel, dim3(grid), dim3(kAttThreads), smem, s, q, k, v, (int)ld, out, (int)H, (int)S, (int)nh,
                                                        c, mask, mask_per_batch ? 1 : 0);
   ICX_LAUNCH_CHECK();
   if (minmax != nullptr) {

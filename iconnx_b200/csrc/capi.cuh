@@ -6,6 +6,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <string>
+#include <utility>
 
 #include "../../include/iconnx_b200.h"
 
@@ -15,6 +16,25 @@ void set_error(const char* fmt, ...);
 void clear_error();
 
 inline cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
+
+// Launch with programmatic stream serialisation: the kernel may be scheduled
+// while its predecessor on the stream finishes; it synchronises on the
+// predecessor itself with griddepcontrol.wait (pdl_wait in common.cuh).
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t s, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
 
 }  // namespace icx
 

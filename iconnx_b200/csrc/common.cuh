@@ -350,6 +350,19 @@ __host__ __device__ constexpr uint32_t idesc_i8(int M, int N, bool a_signed,
          ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
+// ------------------------------------------ programmatic dependent launch
+// Kernels are launched with programmatic stream serialisation (launch_pdl):
+// a kernel may be scheduled while its predecessor on the stream is still
+// running, so every kernel calls pdl_wait() before it reads anything a
+// predecessor wrote (its setup -- barrier init, TMEM allocation, descriptor
+// prefetch -- overlaps the predecessor's tail), and pdl_trigger() to let its
+// own dependents be scheduled once all of its CTAs have started.  Without a
+// programmatic predecessor both are no-ops.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ------------------------------------------------------------ warp helpers
 __device__ __forceinline__ bool elect_one() {
   uint32_t pred = 0;

@@ -16,6 +16,8 @@ __global__ void dequantize_kernel(const T* __restrict__ x, size_t total,
                                   const float* __restrict__ scale,
                                   size_t scale_len, const T* __restrict__ zp,
                                   float* __restrict__ y) {
+  pdl_wait();
+  pdl_trigger();
   const size_t stride = (size_t)gridDim.x * blockDim.x;
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
        i += stride) {
@@ -48,17 +50,17 @@ extern "C" int icx_dequantize_linear(void* stream, const void* d_x, int x_type,
   if (blocks > 148 * 16) blocks = 148 * 16;
   switch (x_type) {
     case ICX_U8:
-      dequantize_kernel<uint8_t><<<(unsigned)blocks, threads, 0, s>>>(
+      launch_pdl(dequantize_kernel<uint8_t>, dim3((unsigned)blocks), dim3(threads), 0, s, 
           static_cast<const uint8_t*>(d_x), total, axis_len, inner, d_scale,
           scale_len, static_cast<const uint8_t*>(d_zp), d_y);
       break;
     case ICX_S8:
-      dequantize_kernel<int8_t><<<(unsigned)blocks, threads, 0, s>>>(
+      launch_pdl(dequantize_kernel<int8_t>, dim3((unsigned)blocks), dim3(threads), 0, s, 
           static_cast<const int8_t*>(d_x), total, axis_len, inner, d_scale,
           scale_len, static_cast<const int8_t*>(d_zp), d_y);
       break;
     default:
-      dequantize_kernel<int32_t><<<(unsigned)blocks, threads, 0, s>>>(
+      launch_pdl(dequantize_kernel<int32_t>, dim3((unsigned)blocks), dim3(threads), 0, s, 
           static_cast<const int32_t*>(d_x), total, axis_len, inner, d_scale,
           scale_len, static_cast<const int32_t*>(d_zp), d_y);
   }

@@ -62,6 +62,8 @@ __global__ void __launch_bounds__(kMinmaxThreads)
     dql_minmax_kernel(const float* __restrict__ x, size_t n,
                       float2* __restrict__ partials,
                       int32_t* __restrict__ rowsum, size_t nrows) {
+  pdl_wait();
+  pdl_trigger();
   float mn = 0.0f, mx = 0.0f;  // the reference seeds the scan with 0.0
   const size_t tid = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
   const size_t stride = (size_t)gridDim.x * blockDim.x;
@@ -189,6 +191,8 @@ __global__ void __launch_bounds__(kQuantThreads, 3)
                         uint8_t* __restrict__ zp_out,
                         int32_t* __restrict__ rowsum, size_t row_len,
                         int vec16) {
+  pdl_wait();
+  pdl_trigger();
   // every warp folds the partials itself (no block barrier) and all lanes
   // derive the f64 scale / zero point in parallel
   DqlParams p;
@@ -275,7 +279,7 @@ static int minmax_blocks(size_t n) {
 int dql_minmax_partials(size_t n) { return minmax_blocks(n); }
 
 int launch_dql_minmax(cudaStream_t s, const float* x, size_t n, float2* partials) {
-  dql_minmax_kernel<<<minmax_blocks(n), kMinmaxThreads, 0, s>>>(x, n, partials, nullptr, 0);
+  launch_pdl(dql_minmax_kernel, dim3(minmax_blocks(n)), dim3(kMinmaxThreads), 0, s, x, n, partials, nullptr, 0);
   ICX_LAUNCH_CHECK();
   return ICX_OK;
 }
@@ -304,7 +308,7 @@ extern "C" int icx_dql_f32_u8(void* stream, const float* d_x, size_t n,
               workspace_bytes, (size_t)blocks * sizeof(float2));
   cudaStream_t s = as_stream(stream);
   const size_t nrows = d_rowsum ? n / row_len : 0;
-  dql_minmax_kernel<<<blocks, kMinmaxThreads, 0, s>>>(
+  launch_pdl(dql_minmax_kernel, dim3(blocks), dim3(kMinmaxThreads), 0, s, 
       d_x, n, static_cast<float2*>(d_workspace), d_rowsum, nrows);
   ICX_LAUNCH_CHECK();
   const bool aligned = ((reinterpret_cast<uintptr_t>(d_x) |
@@ -314,7 +318,7 @@ extern "C" int icx_dql_f32_u8(void* stream, const float* d_x, size_t n,
   size_t qb = (work + kQuantThreads - 1) / kQuantThreads;
   if (qb < 1) qb = 1;
   if (qb > 148 * 3) qb = 148 * 3;
-  dql_quantize_kernel<<<(int)qb, kQuantThreads, 0, s>>>(
+  launch_pdl(dql_quantize_kernel, dim3((int)qb), dim3(kQuantThreads), 0, s, 
       d_x, n, static_cast<const float2*>(d_workspace), blocks, d_y, d_scale,
       d_zp, d_rowsum, row_len ? row_len : 1, vec16);
   ICX_LAUNCH_CHECK();
@@ -341,7 +345,7 @@ extern "C" int icx_dql_quantize_f32_u8(void* stream, const float* d_x, size_t n,
   size_t qb = (work + kQuantThreads - 1) / kQuantThreads;
   if (qb < 1) qb = 1;
   if (qb > 148 * 3) qb = 148 * 3;
-  dql_quantize_kernel<<<(int)qb, kQuantThreads, 0, s>>>(
+  launch_pdl(dql_quantize_kernel, dim3((int)qb), dim3(kQuantThreads), 0, s, 
       d_x, n, reinterpret_cast<const float2*>(d_minmax), n_minmax, d_y, d_scale, d_zp,
       d_rowsum, row_len ? row_len : 1, vec16);
   ICX_LAUNCH_CHECK();
@@ -411,7 +415,7 @@ extern "C" int icx_dql_f32_u8_noalloc(void* stream, const float* d_x, size_t n,
   if (rc) return rc;
   cudaStream_t s = as_stream(stream);
   const size_t nrows = d_rowsum ? n / row_len : 0;
-  dql_minmax_kernel<<<blocks, kMinmaxThreads, 0, s>>>(d_x, n, scratch, d_rowsum, nrows);
+  launch_pdl(dql_minmax_kernel, dim3(blocks), dim3(kMinmaxThreads), 0, s, d_x, n, scratch, d_rowsum, nrows);
   ICX_LAUNCH_CHECK();
   const bool aligned = ((reinterpret_cast<uintptr_t>(d_x) |
                          reinterpret_cast<uintptr_t>(d_y)) & 15) == 0;
@@ -420,7 +424,7 @@ extern "C" int icx_dql_f32_u8_noalloc(void* stream, const float* d_x, size_t n,
   size_t qb = (work + kQuantThreads - 1) / kQuantThreads;
   if (qb < 1) qb = 1;
   if (qb > 148 * 3) qb = 148 * 3;
-  dql_quantize_kernel<<<(int)qb, kQuantThreads, 0, s>>>(
+  launch_pdl(dql_quantize_kernel, dim3((int)qb), dim3(kQuantThreads), 0, s, 
       d_x, n, scratch, blocks, d_y, d_scale, d_zp, d_rowsum, row_len ? row_len : 1, vec16);
   ICX_LAUNCH_CHECK();
   return ICX_OK;

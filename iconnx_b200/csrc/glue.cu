@@ -40,6 +40,8 @@ size_t dtype_size(int t) {
 __global__ void gather_rows_kernel(const float* __restrict__ table, int64_t rows,
                                    const int64_t* __restrict__ idx, size_t n, size_t D,
                                    float* __restrict__ out, int* __restrict__ err) {
+  pdl_wait();
+  pdl_trigger();
   const size_t total = n * D;
   const size_t stride = (size_t)gridDim.x * blockDim.x;
   for (size_t t = (size_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += stride) {
@@ -58,7 +60,7 @@ __global__ void gather_rows_kernel(const float* __restrict__ table, int64_t rows
 int launch_gather_rows(cudaStream_t s, const float* table, int64_t rows, const int64_t* idx,
                        size_t n, size_t D, float* out, int* err) {
   if (n * D == 0) return ICX_OK;
-  gather_rows_kernel<<<elt_blocks(n * D), kEltThreads, 0, s>>>(table, rows, idx, n, D, out, err);
+  launch_pdl(gather_rows_kernel, dim3(elt_blocks(n * D)), dim3(kEltThreads), 0, s, table, rows, idx, n, D, out, err);
   ICX_LAUNCH_CHECK();
   return ICX_OK;
 }
@@ -82,6 +84,8 @@ __device__ __forceinline__ float bin(float a, float b) {
 template <int OP>
 __global__ void binary_same_kernel(const float4* __restrict__ a, const float4* __restrict__ b,
                                    float4* __restrict__ o, size_t n4) {
+  pdl_wait();
+  pdl_trigger();
   const size_t stride = (size_t)gridDim.x * blockDim.x;
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += stride) {
     const float4 x = a[i], y = b[i];
@@ -93,6 +97,8 @@ __global__ void binary_same_kernel(const float4* __restrict__ a, const float4* _
 template <int OP>
 __global__ void binary_rowvec_kernel(const float4* __restrict__ a, const float4* __restrict__ b,
                                      float4* __restrict__ o, size_t n4, size_t d4, int swap) {
+  pdl_wait();
+  pdl_trigger();
   const size_t stride = (size_t)gridDim.x * blockDim.x;
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += stride) {
     const float4 x = a[i], y = b[i % d4];
@@ -107,6 +113,8 @@ __global__ void binary_rowvec_kernel(const float4* __restrict__ a, const float4*
 template <int OP>
 __global__ void binary_scalar_kernel(const float* __restrict__ a, const float* __restrict__ b,
                                      float* __restrict__ o, size_t n, int scalar_is_a) {
+  pdl_wait();
+  pdl_trigger();
   const float sv = scalar_is_a ? a[0] : b[0];
   const float* v = scalar_is_a ? b : a;
   const size_t stride = (size_t)gridDim.x * blockDim.x;
@@ -118,6 +126,8 @@ __global__ void binary_scalar_kernel(const float* __restrict__ a, const float* _
 template <int OP>
 __global__ void binary_bcast32_kernel(const float* __restrict__ a, const float* __restrict__ b,
                                       float* __restrict__ o, unsigned n, BcastShape sh) {
+  pdl_wait();
+  pdl_trigger();
   const unsigned stride = gridDim.x * blockDim.x;
   for (unsigned i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
     unsigned rem = i, ia = 0, ib = 0;
@@ -135,6 +145,8 @@ __global__ void binary_bcast32_kernel(const float* __restrict__ a, const float* 
 template <int OP>
 __global__ void binary_bcast_kernel(const float* __restrict__ a, const float* __restrict__ b,
                                     float* __restrict__ o, size_t n, BcastShape sh) {
+  pdl_wait();
+  pdl_trigger();
   const size_t stride = (size_t)gridDim.x * blockDim.x;
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
     size_t rem = i;
@@ -170,7 +182,7 @@ int launch_binary(cudaStream_t s, int op, const float* a, const std::vector<int6
   if (aligned && n % 4 == 0) {
     if (a_full && b_full) {
 #define ICX_SAME(OPC)                                                                      \
-  binary_same_kernel<OPC><<<elt_blocks(n / 4), kEltThreads, 0, s>>>(                       \
+  launch_pdl(binary_same_kernel<OPC>, dim3(elt_blocks(n / 4)), dim3(kEltThreads), 0, s,                        \
       reinterpret_cast<const float4*>(a), reinterpret_cast<const float4*>(b),              \
       reinterpret_cast<float4*>(out), n / 4)
       switch (op) {
@@ -188,7 +200,7 @@ int launch_binary(cudaStream_t s, int op, const float* a, const std::vector<int6
       const float* m = a_full ? a : b;
       const float* v = a_full ? b : a;
 #define ICX_ROW(OPC)                                                                       \
-  binary_rowvec_kernel<OPC><<<elt_blocks(n / 4), kEltThreads, 0, s>>>(                     \
+  launch_pdl(binary_rowvec_kernel<OPC>, dim3(elt_blocks(n / 4)), dim3(kEltThreads), 0, s,                      \
       reinterpret_cast<const float4*>(m), reinterpret_cast<const float4*>(v),              \
       reinterpret_cast<float4*>(out), n / 4, (size_t)D / 4, swap)
       switch (op) {
@@ -204,7 +216,7 @@ int launch_binary(cudaStream_t s, int op, const float* a, const std::vector<int6
   }
   if (numel(ashape) == 1 || numel(bshape) == 1) {
     const int sa = numel(ashape) == 1 && numel(bshape) != 1;
-#define ICX_SC(OPC) binary_scalar_kernel<OPC><<<elt_blocks(n), kEltThreads, 0, s>>>(a, b, out, n, sa)
+#define ICX_SC(OPC) launch_pdl(binary_scalar_kernel<OPC>, dim3(elt_blocks(n)), dim3(kEltThreads), 0, s, a, b, out, n, sa)
     switch (op) {
       case kAdd: ICX_SC(kAdd); break;
       case kSub: ICX_SC(kSub); break;
@@ -236,9 +248,9 @@ int launch_binary(cudaStream_t s, int op, const float* a, const std::vector<int6
   strides(bshape, sh.sb);
 #define ICX_BC(OPC)                                                                         \
   if (n < (1u << 31))                                                                       \
-    binary_bcast32_kernel<OPC><<<elt_blocks(n), kEltThreads, 0, s>>>(a, b, out, (unsigned)n, sh); \
+    launch_pdl(binary_bcast32_kernel<OPC>, dim3(elt_blocks(n)), dim3(kEltThreads), 0, s, a, b, out, (unsigned)n, sh); \
   else                                                                                      \
-    binary_bcast_kernel<OPC><<<elt_blocks(n), kEltThreads, 0, s>>>(a, b, out, n, sh)
+    launch_pdl(binary_bcast_kernel<OPC>, dim3(elt_blocks(n)), dim3(kEltThreads), 0, s, a, b, out, n, sh)
   switch (op) {
     case kAdd: ICX_BC(kAdd); break;
     case kSub: ICX_BC(kSub); break;
@@ -261,6 +273,8 @@ __global__ void __launch_bounds__(32 * kLnWarps)
     layernorm_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
                      const float* __restrict__ beta, float* __restrict__ y, int rows, int D,
                      float eps, float2* __restrict__ minmax) {
+  pdl_wait();
+  pdl_trigger();
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   float mn = 0.0f, mx = 0.0f;
   const int nv = D / 4;
@@ -347,7 +361,7 @@ int launch_layernorm(cudaStream_t s, const float* x, const float* gamma, const f
   const int blocks = layernorm_partials(rows);
   if (n_minmax) *n_minmax = blocks;
   if (rows == 0) return ICX_OK;
-  layernorm_kernel<<<blocks, 32 * kLnWarps, 0, s>>>(x, gamma, beta, y, (int)rows, (int)D, eps,
+  launch_pdl(layernorm_kernel, dim3(blocks), dim3(32 * kLnWarps), 0, s, x, gamma, beta, y, (int)rows, (int)D, eps,
                                                     reinterpret_cast<float2*>(minmax));
   ICX_LAUNCH_CHECK();
   return ICX_OK;
@@ -357,6 +371,8 @@ int launch_layernorm(cudaStream_t s, const float* x, const float* gamma, const f
 // Row softmax over the last axis, one warp per row (D <= 1024).
 __global__ void softmax_kernel(const float* __restrict__ x, float* __restrict__ y, int rows,
                                int D) {
+  pdl_wait();
+  pdl_trigger();
   const int lane = threadIdx.x & 31;
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (row >= rows) return;
@@ -398,6 +414,8 @@ template <int PER_LANE>
 __global__ void scale_mask_softmax_kernel(const float* __restrict__ x, float* __restrict__ y,
                                           int rows, int D, float c,
                                           const float* __restrict__ mask, int rows_per_batch) {
+  pdl_wait();
+  pdl_trigger();
   const int lane = threadIdx.x & 31;
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (row >= rows) return;
@@ -444,11 +462,11 @@ int launch_scale_mask_softmax(cudaStream_t s, const float* x, float* y, size_t r
   const unsigned grid = (unsigned)((rows + wpb - 1) / wpb);
   const int rpb = (int)(rows_per_batch ? rows_per_batch : rows);
   if (D <= 128)
-    scale_mask_softmax_kernel<4><<<grid, 32 * wpb, 0, s>>>(x, y, (int)rows, (int)D, c, mask, rpb);
+    launch_pdl(scale_mask_softmax_kernel<4>, dim3(grid), dim3(32 * wpb), 0, s, x, y, (int)rows, (int)D, c, mask, rpb);
   else if (D <= 512)
-    scale_mask_softmax_kernel<16><<<grid, 32 * wpb, 0, s>>>(x, y, (int)rows, (int)D, c, mask, rpb);
+    launch_pdl(scale_mask_softmax_kernel<16>, dim3(grid), dim3(32 * wpb), 0, s, x, y, (int)rows, (int)D, c, mask, rpb);
   else
-    scale_mask_softmax_kernel<32><<<grid, 32 * wpb, 0, s>>>(x, y, (int)rows, (int)D, c, mask, rpb);
+    launch_pdl(scale_mask_softmax_kernel<32>, dim3(grid), dim3(32 * wpb), 0, s, x, y, (int)rows, (int)D, c, mask, rpb);
   ICX_LAUNCH_CHECK();
   return ICX_OK;
 }
@@ -457,7 +475,7 @@ int launch_softmax(cudaStream_t s, const float* x, float* y, size_t rows, size_t
   ICX_REQUIRE(D >= 1 && D <= 1024, "Softmax: last dimension %zu unsupported (1..1024)", D);
   if (rows == 0) return ICX_OK;
   const int wpb = 8;
-  softmax_kernel<<<(unsigned)((rows + wpb - 1) / wpb), 32 * wpb, 0, s>>>(x, y, (int)rows, (int)D);
+  launch_pdl(softmax_kernel, dim3((unsigned)((rows + wpb - 1) / wpb)), dim3(32 * wpb), 0, s, x, y, (int)rows, (int)D);
   ICX_LAUNCH_CHECK();
   return ICX_OK;
 }
@@ -472,6 +490,8 @@ struct PermShape {
 template <typename T>
 __global__ void transpose32_kernel(const T* __restrict__ x, T* __restrict__ y, unsigned n,
                                    PermShape ps) {
+  pdl_wait();
+  pdl_trigger();
   const unsigned stride = gridDim.x * blockDim.x;
   for (unsigned i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
     unsigned rem = i, src = 0;
@@ -488,6 +508,8 @@ __global__ void transpose32_kernel(const T* __restrict__ x, T* __restrict__ y, u
 template <typename T>
 __global__ void transpose_kernel(const T* __restrict__ x, T* __restrict__ y, size_t n,
                                  PermShape ps) {
+  pdl_wait();
+  pdl_trigger();
   const size_t stride = (size_t)gridDim.x * blockDim.x;
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
     size_t rem = i;
@@ -522,19 +544,19 @@ int launch_transpose(cudaStream_t s, const void* x, int elem_bytes,
   if (n == 0) return ICX_OK;
   switch (elem_bytes) {
     case 1:
-      transpose_kernel<uint8_t><<<elt_blocks(n), kEltThreads, 0, s>>>(
+      launch_pdl(transpose_kernel<uint8_t>, dim3(elt_blocks(n)), dim3(kEltThreads), 0, s, 
           static_cast<const uint8_t*>(x), static_cast<uint8_t*>(y), n, ps);
       break;
     case 4:
       if (n < (1u << 31))
-        transpose32_kernel<uint32_t><<<elt_blocks(n), kEltThreads, 0, s>>>(
+        launch_pdl(transpose32_kernel<uint32_t>, dim3(elt_blocks(n)), dim3(kEltThreads), 0, s, 
             static_cast<const uint32_t*>(x), static_cast<uint32_t*>(y), (unsigned)n, ps);
       else
-        transpose_kernel<uint32_t><<<elt_blocks(n), kEltThreads, 0, s>>>(
+        launch_pdl(transpose_kernel<uint32_t>, dim3(elt_blocks(n)), dim3(kEltThreads), 0, s, 
             static_cast<const uint32_t*>(x), static_cast<uint32_t*>(y), n, ps);
       break;
     case 8:
-      transpose_kernel<uint64_t><<<elt_blocks(n), kEltThreads, 0, s>>>(
+      launch_pdl(transpose_kernel<uint64_t>, dim3(elt_blocks(n)), dim3(kEltThreads), 0, s, 
           static_cast<const uint64_t*>(x), static_cast<uint64_t*>(y), n, ps);
       break;
     default:
@@ -548,6 +570,8 @@ int launch_transpose(cudaStream_t s, const void* x, int elem_bytes,
 // --------------------------------------------------------------------- Cast
 template <typename S, typename D>
 __global__ void cast_kernel(const S* __restrict__ x, D* __restrict__ y, size_t n) {
+  pdl_wait();
+  pdl_trigger();
   const size_t stride = (size_t)gridDim.x * blockDim.x;
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
     y[i] = (D)x[i];
@@ -561,7 +585,7 @@ int launch_cast(cudaStream_t s, const void* x, int from, void* y, int to, size_t
   }
   const unsigned b = elt_blocks(n);
 #define ICX_CAST(ST, DT) \
-  cast_kernel<ST, DT><<<b, kEltThreads, 0, s>>>(static_cast<const ST*>(x), static_cast<DT*>(y), n)
+  launch_pdl((cast_kernel<ST, DT>), dim3(b), dim3(kEltThreads), 0, s, static_cast<const ST*>(x), static_cast<DT*>(y), n)
   if (to == ICX_F32) {
     switch (from) {
       case ICX_S32: ICX_CAST(int32_t, float); break;  // round to nearest: Rust `as f32`
@@ -600,6 +624,8 @@ __device__ __forceinline__ float erf_as(float v) {
 }
 
 __global__ void erf_kernel(const float* __restrict__ x, float* __restrict__ y, size_t n) {
+  pdl_wait();
+  pdl_trigger();
   const size_t stride = (size_t)gridDim.x * blockDim.x;
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
     y[i] = erf_as(x[i]);
@@ -608,6 +634,8 @@ __global__ void erf_kernel(const float* __restrict__ x, float* __restrict__ y, s
 // The exported erf-GELU subgraph op by op: Div(x, sqrt2) -> Erf -> Add(1)
 // -> Mul(x, .) -> Mul(., 0.5), for GELUs that follow no fusable GEMM.
 __global__ void gelu_kernel(const float* __restrict__ x, float* __restrict__ y, size_t n) {
+  pdl_wait();
+  pdl_trigger();
   const size_t stride = (size_t)gridDim.x * blockDim.x;
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
     const float v = x[i];
@@ -618,14 +646,14 @@ __global__ void gelu_kernel(const float* __restrict__ x, float* __restrict__ y, 
 
 int launch_erf(cudaStream_t s, const float* x, float* y, size_t n) {
   if (n == 0) return ICX_OK;
-  erf_kernel<<<elt_blocks(n), kEltThreads, 0, s>>>(x, y, n);
+  launch_pdl(erf_kernel, dim3(elt_blocks(n)), dim3(kEltThreads), 0, s, x, y, n);
   ICX_LAUNCH_CHECK();
   return ICX_OK;
 }
 
 int launch_gelu(cudaStream_t s, const float* x, float* y, size_t n) {
   if (n == 0) return ICX_OK;
-  gelu_kernel<<<elt_blocks(n), kEltThreads, 0, s>>>(x, y, n);
+  launch_pdl(gelu_kernel, dim3(elt_blocks(n)), dim3(kEltThreads), 0, s, x, y, n);
   ICX_LAUNCH_CHECK();
   return ICX_OK;
 }

@@ -311,6 +311,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // setup above overlaps the previous kernel; its outputs (A, a_scale,
+  // residual, ...) are read only from here on
+  pdl_wait();
+  pdl_trigger();
 
   if (warp == 0) {
     // ---------------------------------------------------------- producer
@@ -641,6 +645,8 @@ template <int EPI>
 __global__ void qgemm_simt_kernel(const void* __restrict__ a, int a_signed,
                                   const void* __restrict__ bt, int b_signed,
                                   const GemmArgs args) {
+  pdl_wait();
+  pdl_trigger();
   const size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int M = args.M, N = args.N, K = args.K;
   if (idx >= (size_t)M * N) return;
@@ -786,7 +792,7 @@ static int launch_tc(cudaStream_t s, const void* a, bool a_signed, const void* b
   int grid = sm_count();
   if (ntiles < grid) grid = ntiles;
   const uint32_t idesc = idesc_i8(kBM, BN, a_signed, b_signed);
-  kern<<<grid, kThreads, C::kSmemBytes, s>>>(ta, tb, tout, tres, args, idesc, tma_store, vec_cols,
+  launch_pdl(kern, dim3(grid), dim3(kThreads), C::kSmemBytes, s, ta, tb, tout, tres, args, idesc, tma_store, vec_cols,
                                              tma_res);
   ICX_LAUNCH_CHECK();
   return ICX_OK;
@@ -835,7 +841,7 @@ static int launch_gemm(cudaStream_t s, const void* a, bool a_signed,
   const size_t blocks = (total + threads - 1) / threads;
   GemmArgs g = args;
   g.minmax = nullptr;
-  qgemm_simt_kernel<EPI><<<(unsigned)blocks, threads, 0, s>>>(a, a_signed, bt, b_signed, g);
+  launch_pdl(qgemm_simt_kernel<EPI>, dim3((unsigned)blocks), dim3(threads), 0, s, a, a_signed, bt, b_signed, g);
   ICX_LAUNCH_CHECK();
   if (EPI != kEpiS32 && args.minmax)
     return launch_dql_minmax(s, static_cast<const float*>(args.out), total, args.minmax);
@@ -848,6 +854,8 @@ static int launch_gemm(cudaStream_t s, const void* a, bool a_signed,
 __global__ void prepare_b_kernel(const uint8_t* __restrict__ b, int b_signed,
                                  int K, int N, uint8_t* __restrict__ bt,
                                  int32_t* __restrict__ colsum) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ uint8_t tile[32][33];
   const int k0 = blockIdx.y * 32, n0 = blockIdx.x * 32;
   const int tx = threadIdx.x, ty = threadIdx.y;  // 32 x 8
@@ -871,6 +879,8 @@ __global__ void prepare_b_kernel(const uint8_t* __restrict__ b, int b_signed,
 // rowsum[m] = sum_k a[m, k] (one warp per row)
 __global__ void rowsum_kernel(const uint8_t* __restrict__ a, int a_signed,
                               int M, int K, int32_t* __restrict__ rowsum) {
+  pdl_wait();
+  pdl_trigger();
   const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (w >= M) return;
@@ -901,7 +911,7 @@ extern "C" int icx_prepare_b(void* stream, const void* d_b, int b_type, size_t K
   cudaStream_t s = as_stream(stream);
   ICX_CUDA(cudaMemsetAsync(d_colsum, 0, N * sizeof(int32_t), s));
   dim3 grid((unsigned)((N + 31) / 32), (unsigned)((K + 31) / 32));
-  prepare_b_kernel<<<grid, dim3(32, 8), 0, s>>>(
+  launch_pdl(prepare_b_kernel, dim3(grid), dim3(dim3(32, 8)), 0, s, 
       static_cast<const uint8_t*>(d_b), b_type == ICX_S8, (int)K, (int)N,
       static_cast<uint8_t*>(d_bt), d_colsum);
   ICX_LAUNCH_CHECK();
@@ -963,7 +973,7 @@ extern "C" int icx_matmul_integer(void* stream, const void* d_a, int a_type,
   if (d_b_zp && M && K) {
     const int threads = 256;
     const size_t blocks = (M * 32 + threads - 1) / threads;
-    rowsum_kernel<<<(unsigned)blocks, threads, 0, as_stream(stream)>>>(
+    launch_pdl(rowsum_kernel, dim3((unsigned)blocks), dim3(threads), 0, as_stream(stream), 
         static_cast<const uint8_t*>(d_a), a_type == ICX_S8, (int)M, (int)K, rowsum);
     ICX_LAUNCH_CHECK();
   } else if (d_b_zp && M) {
@@ -1019,7 +1029,7 @@ extern "C" int icx_matmul_integer_rowsum(void* stream, const void* d_a, int a_ty
   }
   const int threads = 256;
   const size_t blocks = (M * 32 + threads - 1) / threads;
-  rowsum_kernel<<<(unsigned)blocks, threads, 0, s>>>(static_cast<const uint8_t*>(d_a),
+  launch_pdl(rowsum_kernel, dim3((unsigned)blocks), dim3(threads), 0, s, static_cast<const uint8_t*>(d_a),
                                                      a_type == ICX_S8, (int)M, (int)K, d_rowsum);
   ICX_LAUNCH_CHECK();
   return ICX_OK;
