@@ -193,13 +193,24 @@ __global__ void __launch_bounds__(kQuantThreads, 3)
                         int vec16) {
   pdl_wait();
   pdl_trigger();
+  const int lane = threadIdx.x & 31;
+  const size_t warp_g = ((size_t)blockIdx.x * kQuantThreads + threadIdx.x) >> 5;
+  const size_t nwarps = ((size_t)gridDim.x * kQuantThreads) >> 5;
+  const size_t nblk = vec16 ? n / 512 : 0;
+  const float4* x4 = reinterpret_cast<const float4*>(x);
+  // this warp's first 512 elements are requested before the partials are
+  // folded, so the fold and the f64 scale overlap the load latency
+  float4 nv[4];
+  if (warp_g < nblk) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) nv[j] = __ldg(x4 + warp_g * 128 + 32 * j + lane);
+  }
   // every warp folds the partials itself (no block barrier) and all lanes
   // derive the f64 scale / zero point in parallel
   DqlParams p;
   {
-    const int l = threadIdx.x & 31;
     float mn = 0.0f, mx = 0.0f;
-    for (int i = l; i < nparts; i += 32) {
+    for (int i = lane; i < nparts; i += 32) {
       const float2 v = partials[i];
       mn = fminf(mn, v.x);
       mx = fmaxf(mx, v.y);
@@ -211,9 +222,6 @@ __global__ void __launch_bounds__(kQuantThreads, 3)
       *zp_out = (uint8_t)p.zpf;
     }
   }
-  const int lane = threadIdx.x & 31;
-  const size_t warp_g = ((size_t)blockIdx.x * kQuantThreads + threadIdx.x) >> 5;
-  const size_t nwarps = ((size_t)gridDim.x * kQuantThreads) >> 5;
 
   size_t done = 0;
   if (vec16) {
@@ -222,15 +230,8 @@ __global__ void __launch_bounds__(kQuantThreads, 3)
     // coalesced 128-byte stores of the packed u8 words.  A 4-element word
     // never straddles a row because the host selects this path only when
     // row_len % 4 == 0 (or no row sums are requested).
-    const size_t nblk = n / 512;
-    const float4* x4 = reinterpret_cast<const float4*>(x);
     uint32_t* y4 = reinterpret_cast<uint32_t*>(y);
     // the next iteration's four loads are issued before this one is processed
-    float4 nv[4];
-    if (warp_g < nblk) {
-#pragma unroll
-      for (int j = 0; j < 4; ++j) nv[j] = __ldg(x4 + warp_g * 128 + 32 * j + lane);
-    }
     for (size_t blk = warp_g; blk < nblk; blk += nwarps) {
       const size_t base4 = blk * 128;
       float4 v[4];
