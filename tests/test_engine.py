@@ -102,8 +102,9 @@ def test_shape_guard_and_dtype_errors():
 
 @gpu
 @pytest.mark.parametrize("cfg,batch,seq", [
-    (graphs.BertConfig(layers=2), 2, 16),
-    (graphs.BertConfig(layers=1, per_channel=True, token_type=True), 2, 32),
+    (graphs.BertConfig(layers=2, w_scale=graphs.REALISTIC_W_SCALE), 2, 16),
+    (graphs.BertConfig(layers=1, per_channel=True, token_type=True,
+                       w_scale=graphs.REALISTIC_W_SCALE), 2, 32),
 ])
 def test_encoder_matches_cpu_interpreter(cfg, batch, seq):
     ex, cpu, out = both(graphs.build_bert, cfg, batch, seq)
@@ -120,6 +121,26 @@ def test_encoder_matches_cpu_interpreter(cfg, batch, seq):
     assert len([s for s in plan if s.startswith("Attention ")]) == cfg.layers
     assert not any(s.startswith(("Transpose", "Softmax", "MatMul ")) for s in plan)
     assert len([s for s in plan if s.startswith("QuantLinear+Residual")]) == 2 * cfg.layers
+
+
+@gpu
+@pytest.mark.parametrize("cfg", [graphs.BertConfig(layers=1),
+                                 graphs.BertConfig(layers=1, per_channel=True, token_type=True)])
+def test_encoder_at_config_weight_scale(cfg):
+    """The configs' own weight scale (0.01, per-channel [0.005, 0.02]): scores
+    of order 10^3 make softmax nearly one-hot, and where two keys nearly tie,
+    any fp32 reordering of the score sums (this tensor-core attention, the
+    reference's cuBLAS path, numpy) moves the context by ~1e-3, which can
+    push a requantised value across a u8 boundary in that token's row.  So:
+    every row matches to 5e-2 except at most 10% of the rows, and the median
+    row agrees to 1e-4."""
+    ex, cpu, out = both(graphs.build_bert, cfg, 2, 32)
+    inp = graphs.bert_inputs(2, 32)
+    g = ex.run(inp, [out])[out]
+    r = cpu.run(inp, [out])[out]
+    row_err = np.abs(g - r).max(axis=-1)
+    assert np.mean(row_err > 5e-2) <= 0.1, row_err
+    assert np.median(row_err) < 1e-4, np.median(row_err)
 
 
 @gpu
