@@ -447,6 +447,15 @@ class Engine {
     skip_.clear();
     dql_mode_.clear();
     minmax_count_.clear();
+    // initializers derived at the previous compile are derived again
+    for (auto& nm : folded_) {
+      auto it = inits_.find(nm);
+      if (it != inits_.end()) {
+        if (it->second->dev) cudaFree(it->second->dev);
+        inits_.erase(it);
+      }
+    }
+    folded_.clear();
     for (auto& nm : inputs_) {
       Val v;
       v.dtype = input_defs_[nm].first;
@@ -468,6 +477,7 @@ class Engine {
       rc = infer(nodes_[idx], idx);
       if (rc) return rc;
     }
+    fold_constants();
     for (auto& o : outputs)
       if (!vals_.count(o)) {
         set_error("requested output '%s' is not produced by the graph", o.c_str());
@@ -623,11 +633,11 @@ class Engine {
     } else if (op == "Gather") {
       if (!need(0) || !need(1)) return fail(n, "needs data and indices");
       if (n.geti("axis", 0) != 0) return fail(n, "only axis 0 is supported");
-      if (in[0]->dtype != ICX_F32 || in[1]->dtype != ICX_S64)
-        return fail(n, "data must be Float32 and indices Int64");
+      if (in[1]->dtype != ICX_S64) return fail(n, "indices must be Int64");
+      if (in[0]->dtype == ICX_BOOL) return fail(n, "Bool data unsupported");
       Shape o = in[1]->shape;
       o.insert(o.end(), in[0]->shape.begin() + 1, in[0]->shape.end());
-      out_val(idx, 0, ICX_F32, o);
+      out_val(idx, 0, in[0]->dtype, o);
     } else if (op == "Reshape" || op == "Unsqueeze" || op == "Squeeze") {
       if (!need(0)) return fail(n, "needs data");
       Shape o;
@@ -731,6 +741,72 @@ class Engine {
     return -1;
   }
 
+  // A derived initializer (constant folding, weight conversion), rebuilt at
+  // every compile.
+  Init* add_derived(const std::string& name, int dtype, const Shape& shape,
+                    std::vector<uint8_t> data) {
+    auto in = std::make_unique<Init>();
+    in->dtype = dtype;
+    in->shape = shape;
+    in->data = std::move(data);
+    Init* p = in.get();
+    inits_[name] = std::move(in);
+    folded_.insert(name);
+    Val& v = vals_[name];
+    v.dtype = dtype;
+    v.shape = shape;
+    v.init = p;
+    v.producer = -1;
+    v.alias.clear();
+    return p;
+  }
+
+  // Nodes whose data input is an initializer and that only move or relabel
+  // bytes (Transpose, Reshape, Unsqueeze, Squeeze, Identity) run once here on
+  // the host: quantised exports store weights as `W_transposed_quantized`
+  // behind a Transpose, and the folded weight is what the QuantLinear
+  // fusion needs.
+  void fold_constants() {
+    for (int idx : order_) {
+      const NodeDef& n = nodes_[idx];
+      const bool relabel = n.op == "Reshape" || n.op == "Unsqueeze" || n.op == "Squeeze" ||
+                           n.op == "Identity";
+      if (!relabel && n.op != "Transpose") continue;
+      if (n.in.empty() || n.out.size() != 1) continue;
+      const Init* x = init_of(n.in[0]);
+      if (!x || is_requested(n.out[0])) continue;
+      const Val& ov = vals_[n.out[0]];
+      const Shape oshape = ov.shape;
+      std::vector<uint8_t> data;
+      if (relabel) {
+        data = x->data;
+      } else {
+        const size_t es = dtype_size(x->dtype);
+        const Shape& s = x->shape;
+        const size_t r = s.size();
+        std::vector<int64_t> perm;
+        if (const auto* p = n.getints("perm")) perm = *p;
+        else for (int64_t d = (int64_t)r - 1; d >= 0; --d) perm.push_back(d);
+        std::vector<int64_t> istride(r, 1);
+        for (int64_t d = (int64_t)r - 2; d >= 0; --d) istride[d] = istride[d + 1] * s[d + 1];
+        const int64_t total = numel(s);
+        data.resize((size_t)total * es);
+        std::vector<int64_t> oi(r, 0);
+        for (int64_t t = 0; t < total; ++t) {
+          int64_t src = 0;
+          for (size_t k = 0; k < r; ++k) src += oi[k] * istride[perm[k]];
+          memcpy(data.data() + (size_t)t * es, x->data.data() + (size_t)src * es, es);
+          for (int64_t k = (int64_t)r - 1; k >= 0; --k) {
+            if (++oi[k] < oshape[k]) break;
+            oi[k] = 0;
+          }
+        }
+      }
+      add_derived(n.out[0], x->dtype, oshape, std::move(data));
+      skip_.insert(idx);
+    }
+  }
+
   void fuse() {
     for (int idx : order_) {
       const NodeDef& mm = nodes_[idx];
@@ -740,11 +816,28 @@ class Engine {
       const NodeDef& d = nodes_[dq];
       if (mm.in.size() < 3 || mm.in[2] != d.out[2]) continue;  // a_zp must be the DQL's zp
       const Init* w = init_of(mm.in[1]);
-      if (!w || w->dtype != ICX_S8 || w->shape.size() != 2 || w->shape[0] % 16) continue;
-      std::string bz;
-      if (mm.in.size() > 3 && !mm.in[3].empty()) {
-        const Init* z = init_of(mm.in[3]);
-        if (!z || z->dtype != ICX_S8) continue;
+      if (!w || (w->dtype != ICX_S8 && w->dtype != ICX_U8) || w->shape.size() != 2 || w->shape[0] % 16)
+        continue;
+      std::string wname = mm.in[1], bz;
+      const Init* z = (mm.in.size() > 3 && !mm.in[3].empty()) ? init_of(mm.in[3]) : nullptr;
+      if (mm.in.size() > 3 && !mm.in[3].empty() && (!z || z->dtype != w->dtype)) continue;
+      if (w->dtype == ICX_U8) {
+        // u8 weights w with zero point z (0 when absent): w - z = (w ^ 0x80) - (z ^ 0x80)
+        // exactly, with both sides of the right-hand difference in s8
+        wname = mm.in[1] + "#s8";
+        if (!init_of(wname)) {
+          std::vector<uint8_t> d = w->data;
+          for (auto& b : d) b ^= 0x80;
+          add_derived(wname, ICX_S8, w->shape, std::move(d));
+        }
+        bz = (z ? mm.in[3] : mm.in[1]) + "#zp_s8";
+        if (!init_of(bz)) {
+          std::vector<uint8_t> d = z ? z->data : std::vector<uint8_t>(1, 0);
+          for (auto& b : d) b ^= 0x80;
+          add_derived(bz, ICX_S8, z ? z->shape : Shape{}, std::move(d));
+        }
+        w = init_of(wname);
+      } else if (z) {
         bz = mm.in[3];
       }
       std::vector<int> chain{idx};
@@ -768,7 +861,7 @@ class Engine {
       f.q = d.out[0];
       f.s = d.out[1];
       f.z = d.out[2];
-      f.w = mm.in[1];
+      f.w = wname;
       f.ws = *ws;
       f.bz = bz;
       std::string cur = nodes_[mul].out[0];
@@ -1517,16 +1610,15 @@ class Engine {
         return launch_layernorm(s, xp, g, b, static_cast<float*>(out), rows, D, eps, mm, mmc);
       }, 1);
     } else if (op == "Gather") {
-      const Init* data = init_of(n.in[0]);
-      const float* table = static_cast<const float*>(ptr(0));
+      const void* table = ptr(0);
+      const int es = (int)dtype_size(vals_[n.in[0]].dtype);
       const int64_t rows = shp(0)[0];
       const size_t D = (size_t)(numel(shp(0)) / (rows ? rows : 1));
       const int64_t* ids = static_cast<const int64_t*>(ptr(1));
       const size_t cnt = (size_t)numel(shp(1));
       int* err = err_flag_;
-      (void)data;
       add_step(n, op, o0, [=](cudaStream_t s) {
-        return launch_gather_rows(s, table, rows, ids, cnt, D, static_cast<float*>(out), err);
+        return launch_gather_rows(s, table, es, rows, ids, cnt, D, out, err);
       }, 1);
     } else if (op == "Transpose") {
       const void* xp = ptr(0);
@@ -1630,6 +1722,7 @@ class Engine {
   std::map<int, FusedQL> fused_;
   std::map<int, FusedAttn> attn_;
   std::set<int> skip_;
+  std::set<std::string> folded_;  // initializers derived at compile (folded / converted)
   std::map<int, int> dql_mode_;
   int n_slots_ = 0;
   std::vector<int> minmax_count_;

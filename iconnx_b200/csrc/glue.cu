@@ -35,11 +35,14 @@ size_t dtype_size(int t) {
 }
 
 // ------------------------------------------------------------------ Gather
-// out[i, :] = table[idx[i], :] (axis 0, negative indices wrap, rows of D).
-// Out-of-range indices write zeros and raise *err (checked by the host).
-__global__ void gather_rows_kernel(const float* __restrict__ table, int64_t rows,
+// out[i, :] = table[idx[i], :] (axis 0, negative indices wrap, rows of D
+// elements of type T: f32 embeddings, or the u8 / s8 tables of quantised
+// exports).  Out-of-range indices write zeros and raise *err (checked by the
+// host).
+template <typename T>
+__global__ void gather_rows_kernel(const T* __restrict__ table, int64_t rows,
                                    const int64_t* __restrict__ idx, size_t n, size_t D,
-                                   float* __restrict__ out, int* __restrict__ err) {
+                                   T* __restrict__ out, int* __restrict__ err) {
   pdl_wait();
   pdl_trigger();
   const size_t total = n * D;
@@ -50,17 +53,34 @@ __global__ void gather_rows_kernel(const float* __restrict__ table, int64_t rows
     if (r < 0) r += rows;
     if (r < 0 || r >= rows) {
       if (d == 0 && err) atomicExch(err, 1);
-      out[t] = 0.0f;
+      out[t] = T(0);
       continue;
     }
     out[t] = table[(size_t)r * D + d];
   }
 }
 
-int launch_gather_rows(cudaStream_t s, const float* table, int64_t rows, const int64_t* idx,
-                       size_t n, size_t D, float* out, int* err) {
+int launch_gather_rows(cudaStream_t s, const void* table, int elem_bytes, int64_t rows,
+                       const int64_t* idx, size_t n, size_t D, void* out, int* err) {
   if (n * D == 0) return ICX_OK;
-  launch_pdl(gather_rows_kernel, dim3(elt_blocks(n * D)), dim3(kEltThreads), 0, s, table, rows, idx, n, D, out, err);
+  const dim3 g(elt_blocks(n * D)), b(kEltThreads);
+  switch (elem_bytes) {
+    case 1:
+      launch_pdl(gather_rows_kernel<uint8_t>, g, b, 0, s, static_cast<const uint8_t*>(table), rows,
+                 idx, n, D, static_cast<uint8_t*>(out), err);
+      break;
+    case 4:
+      launch_pdl(gather_rows_kernel<uint32_t>, g, b, 0, s, static_cast<const uint32_t*>(table), rows,
+                 idx, n, D, static_cast<uint32_t*>(out), err);
+      break;
+    case 8:
+      launch_pdl(gather_rows_kernel<uint64_t>, g, b, 0, s, static_cast<const uint64_t*>(table), rows,
+                 idx, n, D, static_cast<uint64_t*>(out), err);
+      break;
+    default:
+      set_error("Gather: element size %d unsupported", elem_bytes);
+      return ICX_ERR_UNSUPPORTED;
+  }
   ICX_LAUNCH_CHECK();
   return ICX_OK;
 }

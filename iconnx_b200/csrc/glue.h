@@ -15,8 +15,8 @@ enum BinaryOp { kAdd = 0, kSub = 1, kMul = 2, kDiv = 3 };
 
 size_t dtype_size(int t);
 
-int launch_gather_rows(cudaStream_t s, const float* table, int64_t rows, const int64_t* idx,
-                       size_t n, size_t D, float* out, int* err);
+int launch_gather_rows(cudaStream_t s, const void* table, int elem_bytes, int64_t rows,
+                       const int64_t* idx, size_t n, size_t D, void* out, int* err);
 int launch_binary(cudaStream_t s, int op, const float* a, const std::vector<int64_t>& ashape,
                   const float* b, const std::vector<int64_t>& bshape, float* out,
                   const std::vector<int64_t>& oshape);

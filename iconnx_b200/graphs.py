@@ -271,6 +271,57 @@ def attention_reference(q, k, v, heads: int, mask_bias=None) -> np.ndarray:
     return (p @ split(v)).transpose(0, 2, 1, 3).reshape(B, S, H)
 
 
+def _u8(shape, seed, lo=0, hi=255):
+    return synth.int8_uniform(shape, seed, lo - 128, hi - 128).view(np.uint8) ^ np.uint8(0x80)
+
+
+def build_quantized_export(g, batch: int = 2, seq: int = 64, hidden: int = 768, ffn: int = 3072,
+                           vocab: int = 1000, w_scale: float = REALISTIC_W_SCALE) -> tuple:
+    """The layout of dynamically quantised transformer exports (the
+    "_quantized" ONNX files of Transformers.js / Optimum): a u8 embedding
+    table read with Gather and DequantizeLinear, and Linears whose u8 weights
+    are stored transposed ("<name>_transposed_quantized" [N, K]) behind a
+    runtime Transpose, with u8 weight zero points (scalar for the first
+    Linear, per output column for the second).  Input input_ids [batch, seq];
+    outputs (embedding f32, FFN1+GELU f32, FFN2 f32)."""
+    nm = _Namer()
+    g.add_input("input_ids", [batch, seq], np.int64)
+    g.add_initializer("emb_quantized", _u8((vocab, hidden), 31))
+    g.add_initializer("emb_scale", np.array(0.02, np.float32))
+    g.add_initializer("emb_zero_point", np.array(128, np.uint8))
+    g.add_node("emb_gather", "Gather", ["emb_quantized", "input_ids"], ["emb_q"])
+    g.add_node("emb_dq", "DequantizeLinear", ["emb_q", "emb_scale", "emb_zero_point"], ["emb"])
+
+    def linear(x, K, N, seed, per_col, gelu):
+        wt = nm("W_transposed_quantized")
+        g.add_initializer(wt, _u8((N, K), seed))
+        w = nm("W")
+        g.add_node(nm("transpose"), "Transpose", [wt], [w], {"perm": [1, 0]})
+        sn, zn = nm("W_scale"), nm("W_zero_point")
+        if per_col:
+            g.add_initializer(sn, synth.uniform_f32((N,), 0.5 * w_scale, 2.0 * w_scale, seed + 1))
+            g.add_initializer(zn, _u8((N,), seed + 2, 120, 136))
+        else:
+            g.add_initializer(sn, np.array(w_scale, np.float32))
+            g.add_initializer(zn, np.array(131, np.uint8))
+        q, s_, z = dql(g, x, nm)
+        acc, cast, sc, o = nm("acc"), nm("cast"), nm("scale"), nm("deq")
+        g.add_node(nm("mmi"), "MatMulInteger", [q, w, z, zn], [acc])
+        g.add_node(nm("cast"), "Cast", [acc], [cast], {"to": 1})
+        g.add_node(nm("mul"), "Mul", [s_, sn], [sc])
+        g.add_node(nm("mul"), "Mul", [cast, sc], [o])
+        bn, ob = nm("bias"), nm("biased")
+        g.add_initializer(bn, synth.normal((N,), 0.02, seed + 3))
+        g.add_node(nm("add"), "Add", [o, bn], [ob])
+        return gelu_subgraph(g, ob, nm) if gelu else ob
+
+    h = linear("emb", hidden, ffn, 40, False, True)
+    y = linear(h, ffn, hidden, 50, True, False)
+    g.add_node("out_h", "Identity", [h], ["ffn1"])
+    g.add_node("out_y", "Identity", [y], ["ffn2"])
+    return "emb", "ffn1", "ffn2"
+
+
 def layernorm(g, x: str, nm: _Namer, H: int, seed: int, eps: float) -> str:
     gn, bn, y = nm("ln_gamma"), nm("ln_beta"), nm("ln")
     g.add_initializer(gn, (1.0 + synth.normal((H,), 0.02, seed + 1000)).astype(np.float32))

@@ -175,3 +175,52 @@ def test_replay_rereads_last_inputs():
     torch.cuda.synchronize()
     np.testing.assert_array_equal(ex.fetch(out), ref)
     np.testing.assert_array_equal(ex.run(inp, [out])[out], ref)
+
+
+def test_quantized_export_layout_on_cpu_interpreter():
+    """The export layout runs through the CPU interpreter (u8 Gather,
+    DequantizeLinear, Transpose of u8 weights, u8 weight zero points)."""
+    cpu = CpuGraph()
+    e, h, y = graphs.build_quantized_export(cpu, batch=1, seq=8, hidden=128, ffn=256)
+    out = cpu.run({"input_ids": synth.token_ids((1, 8), 6, 1000)}, [e, h, y])
+    assert out[e].dtype == np.float32 and out[y].shape == (1, 8, 128)
+
+
+@gpu
+def test_quantized_export_layout_fuses_and_matches():
+    """u8 embedding Gather + DequantizeLinear (bit-exact), Transpose of the u8
+    `_transposed_quantized` weights folded at compile, u8 weights with scalar
+    and per-column u8 zero points converted exactly to s8 (w ^ 0x80, z ^ 0x80)
+    and run as fused QuantLinears: FFN1+GELU within 1e-5 of the interpreter,
+    FFN2 within the bound of test_config2_ffn_block."""
+    ex, cpu, outs = both(graphs.build_quantized_export, batch=2, seq=64)
+    e, h, y = outs
+    inp = {"input_ids": synth.token_ids((2, 64), 6, 1000)}
+    g = ex.run(inp, list(outs))
+    r = cpu.run(inp, list(outs))
+    np.testing.assert_array_equal(g[e].view(np.uint32), r[e].view(np.uint32))
+    np.testing.assert_allclose(g[h], r[h], atol=1e-5, rtol=0)
+    np.testing.assert_allclose(g[y], r[y], atol=2e-3, rtol=1e-4)
+    plan = ex.plan()
+    assert len([s for s in plan if s.startswith("QuantLinear")]) == 2, plan
+    assert not any(s.startswith("Transpose") for s in plan), plan
+
+
+@gpu
+def test_quantized_export_through_onnx_file(tmp_path):
+    """The same graph written as a .onnx file and loaded with
+    OnnxParser.parse_file / GpuGraphExecutor.from_model."""
+    from iconnx_b200.engine import GpuGraphExecutor
+    from iconnx_b200.onnx import GraphRecorder, OnnxParser, save_model
+    rec = GraphRecorder()
+    outs = graphs.build_quantized_export(rec, batch=2, seq=16, hidden=128, ffn=256)
+    path = tmp_path / "export.onnx"
+    save_model(path, rec, list(outs))
+    ex = GpuGraphExecutor.from_model(OnnxParser.parse_file(path))
+    cpu = CpuGraph()
+    graphs.build_quantized_export(cpu, batch=2, seq=16, hidden=128, ffn=256)
+    inp = {"input_ids": synth.token_ids((2, 16), 7, 1000)}
+    g = ex.run(inp, list(outs))
+    r = cpu.run(inp, list(outs))
+    np.testing.assert_array_equal(g[outs[0]].view(np.uint32), r[outs[0]].view(np.uint32))
+    np.testing.assert_allclose(g[outs[1]], r[outs[1]], atol=1e-5, rtol=0)
