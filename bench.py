@@ -281,6 +281,23 @@ def _torch_graph_replay(wl):
     return g.replay, torch.cuda.current_stream(wl.device)
 
 
+def _int_mm_reference(torch, dev, stream, n=8192, reps=20):
+    """An achievable int8 tensor-core reference measured on this box: cuBLASLt's
+    s8 x s8 -> s32 GEMM (torch._int_mm) at n^3, CUDA events, back-to-back."""
+    a = torch.randint(-127, 128, (n, n), dtype=torch.int8, device=dev)
+    b = torch.randint(-127, 128, (n, n), dtype=torch.int8, device=dev)
+    for _ in range(3):
+        torch._int_mm(a, b)
+    s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s_ev.record(stream)
+    for _ in range(reps):
+        torch._int_mm(a, b)
+    e_ev.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = s_ev.elapsed_time(e_ev) / reps
+    return {"tops": 2.0 * n ** 3 / (ms / 1e3) / 1e12, "shape": f"{n}x{n}x{n}", "ms": ms}
+
+
 def _ffn_gemm_probe(torch, device, M, K=768, N=3072):
     """The GELU-fused FFN1 GEMM (dominant kernel of every encoder layer)."""
     from iconnx_b200 import ops, synth
@@ -300,7 +317,7 @@ def _ffn_gemm_probe(torch, device, M, K=768, N=3072):
 class EncoderWorkload:
     """Configs 3 / 4: an int8 encoder through GpuGraphExecutor."""
 
-    def __init__(self, device, kind="distilbert", seed_base=0):
+    def __init__(self, device, kind="distilbert", seed_base=0, batch=None):
         import torch
         from iconnx_b200 import graphs
         from iconnx_b200.engine import GpuGraphExecutor
@@ -312,6 +329,9 @@ class EncoderWorkload:
         else:
             self.cfg, self.batch, self.seq = graphs.BERT_BASE, 64, 512
             self.model = "BERT-base (12 layers, int8 Linears, per-column scale + zero point)"
+        self.global_batch = self.batch
+        if batch is not None:
+            self.batch = batch
         self.M = self.batch * self.seq
         self.ex = GpuGraphExecutor.new(device.index or 0)
         self.out = graphs.build_bert(self.ex, self.cfg, self.batch, self.seq)
@@ -357,8 +377,9 @@ class EncoderWorkload:
 
 
 WORKLOADS = {"ffn": FfnWorkload, "sweep": SweepWorkload,
-             "distilbert": lambda dev, seed_base=0: EncoderWorkload(dev, "distilbert", seed_base),
-             "bert": lambda dev, seed_base=0: EncoderWorkload(dev, "bert", seed_base)}
+             "distilbert": lambda dev, seed_base=0, batch=None: EncoderWorkload(dev, "distilbert",
+                                                                                 seed_base, batch),
+             "bert": lambda dev, seed_base=0, batch=None: EncoderWorkload(dev, "bert", seed_base, batch)}
 
 
 # ------------------------------------------------------------------ helpers
@@ -481,6 +502,9 @@ def main():
     ap.add_argument("--workload", default="distilbert", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--scaling", default="weak", choices=["weak", "strong"],
+                    help="weak: every GPU runs the config's batch; strong (encoders): the "
+                         "config's batch is split across the GPUs")
     ap.add_argument("--kernel", choices=["ffn1", "gemm", "quant", "residual", "attention"],
                     help="launch one kernel of the path a few times and exit (ncu captures)")
     ap.add_argument("--shape", default="4096,768,3072",
@@ -504,7 +528,14 @@ def main():
         import torch.distributed as dist
         dist.init_process_group("nccl", device_id=dev)
         pg = dist
-    wl = WORKLOADS[args.workload](dev, seed_base=1000 * rank)
+    strong = args.scaling == "strong" and args.workload in ("distilbert", "bert")
+    if strong:
+        full = 32 if args.workload == "distilbert" else 64
+        if full % world:
+            raise SystemExit(f"--scaling strong: batch {full} does not split over {world} GPUs")
+        wl = WORKLOADS[args.workload](dev, seed_base=1000 * rank, batch=full // world)
+    else:
+        wl = WORKLOADS[args.workload](dev, seed_base=1000 * rank)
     stream = torch.cuda.current_stream(dev)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     if not hasattr(wl, "launches_per_step"):
@@ -591,6 +622,9 @@ def main():
     else:
         roof = {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                 "frac": gbs / peaks["hbm_gbs"], "peak_source": f"{peak_kind} hbm_gbs"}
+    if wl.name == "sweep":
+        roof["cublaslt_int8"] = _int_mm_reference(torch, dev, stream)
+        roof["frac_of_cublaslt_int8"] = tops / roof["cublaslt_int8"]["tops"]
     traffic = roofline_traffic(kdesc)
     roof.update({"traffic": traffic, "traffic_note": "ncu dram read+write bytes per launch (profiles/), "
                  "scaled by rows where the capture used a smaller M", "algorithmic_bytes": bytes_alg,
@@ -599,7 +633,7 @@ def main():
 
     line = {"metric": METRIC, "value": value, "unit": wl.unit, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "higher_is_better": True, "scaling": "strong" if strong else "weak", "vs_baseline": None,
             "dtype": "u8xs8->s32, f32 epilogue", "data": "synthetic (seeded)",
             "config": {"workload": wl.name, "M_per_gpu": wl.M,
                        "l2": "256 MiB flush between timed steps",
@@ -614,6 +648,8 @@ def main():
     if isinstance(wl, EncoderWorkload):
         line["config"].update({"model": wl.model, "global_batch": wl.batch * world,
                                "seq_len": wl.seq, "batch_per_gpu": wl.batch})
+        if strong:
+            line["config"]["parallelism"] += f"; strong scaling of the config's batch {wl.global_batch}"
         line["int8_gemm_tops_in_step"] = wl.gemm_ops / (total_ms / args.steps / 1e3) / 1e12
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         from oracle import oracle
