@@ -209,11 +209,21 @@ __global__ void __launch_bounds__(kQuantThreads, 3)
   // derive the f64 scale / zero point in parallel
   DqlParams p;
   {
+    // eight independent loads in flight per lane (a dependent loop would pay
+    // one L2 round trip per 32 partials)
     float mn = 0.0f, mx = 0.0f;
-    for (int i = lane; i < nparts; i += 32) {
-      const float2 v = partials[i];
-      mn = fminf(mn, v.x);
-      mx = fmaxf(mx, v.y);
+    for (int i0 = 0; i0 < nparts; i0 += 256) {
+      float2 v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int i = i0 + 32 * u + lane;
+        v[u] = i < nparts ? partials[i] : make_float2(0.0f, 0.0f);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        mn = fminf(mn, v[u].x);
+        mx = fmaxf(mx, v[u].y);
+      }
     }
     warp_minmax(mn, mx);
     p = dql_params(mn, mx);
