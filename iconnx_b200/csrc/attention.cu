@@ -208,46 +208,65 @@ __global__ void __launch_bounds__(kAttThreads)
 // hi*hi + hi*lo + lo*hi (three kind::tf32 MMAs); errors there are not
 // amplified (p <= 1).
 //
-// 8 warps, two CTAs per SM (84 KB shared memory, 256 TMEM columns each), so
-// one CTA's MMA waits and load latencies overlap the other's work.  Query
-// row r is TMEM lane r; warp w reads lanes 32*(w%4) .. +31 (the quadrant a
-// warp may access) and owns columns 32*(w/4) .. +31 of every 64-key tile and
-// of the context, so two warps share a row and exchange its running max /
-// sum through shared memory.  Per 64-key tile:
+// Tiling (AttTc below): KT keys per tile, NW warps per CTA; query row r is
+// TMEM lane r and warp w reads lanes 32*(w%4) .. +31 (the quadrant a warp
+// may access); with NW = 8 two warps share each row (columns split, row max
+// and sum exchanged through shared memory).  The default <32, 4> runs three
+// CTAs per SM, one warp per row block, so one CTA's MMA waits and load
+// latencies overlap the others' work.  Per key tile:
 //   1. all threads slice the tile's K rows (bytes, [key][slice pair][d],
 //      loaded into registers during the previous tile) into the
 //      128-byte-swizzled K-major layout the MMA reads;
-//   2. thread 0 issues the 20 integer MMAs of S (M=128, N=64, K=32) into TMEM
-//      columns [64 L, 64 L + 64) for L = 0..3; meanwhile all threads load V,
+//   2. thread 0 issues the 20 integer MMAs of S (M=128, N=KT, K=32) into TMEM
+//      columns [KT L, KT L + KT) for L = 0..3; meanwhile all threads load V,
 //      split it into tf32 hi / lo and store it transposed ([d][key]);
-//   3. each thread combines its 32 scores, applies Div(c) and Add(mask); the
-//      row max over the two warps gives the online-softmax update; the
-//      unnormalised probabilities P, split hi / lo, are written back into
-//      TMEM columns [0,64) / [64,128) (the consumed score columns);
-//   4. thread 0 issues O_tile = P V (M=128, N=64, K=64 keys; A = P read from
-//      TMEM, B = V^T from shared memory) into columns [128,192); meanwhile
-//      all threads load the next K tile; each thread rescales its 32
+//   3. each thread combines its scores, applies Div(c) and Add(mask), takes
+//      the row max (online softmax) and writes the unnormalised
+//      probabilities P, split hi / lo, back into TMEM columns [0,KT) /
+//      [KT,2KT) (the consumed score columns);
+//   4. thread 0 issues O_tile = P V (M=128, N=64, K=KT keys; A = P read from
+//      TMEM, B = V^T from shared memory) into columns [2KT, 2KT+64);
+//      meanwhile all threads load the next K tile; each thread rescales its
 //      accumulator columns and adds its O_tile slice.
 constexpr int kTcQ = 128;
-constexpr int kTcK = 64;
-constexpr int kTcThreads = 256;
-constexpr int kTcCols = 32;           // score / context columns per thread
-constexpr int kQAtom = kTcQ * 128;    // one 128-byte-wide column block of 128 rows
-constexpr int kKAtom = kTcK * 128;    // one 128-byte-wide column block of 64 rows
-constexpr int kOffQs = 0;                              // Q slices: 2 blocks (slices 0|1, 2|3)
-constexpr int kOffKs = kOffQs + 2 * kQAtom;            // K slices: 2 blocks
-constexpr int kOffVh = kOffKs + 2 * kKAtom;            // V^T hi / lo: 2 blocks each
-constexpr int kOffVl = kOffVh + 2 * kKAtom;
-constexpr int kOffRed = kOffVl + 2 * kKAtom;           // [2][128] partial max, [2][128] partial sum
-constexpr int kOffScale = kOffRed + 2 * 2 * kTcQ * 4;  // 2^(nq-1) per query row, 2^(nk-1) per key
-constexpr int kOffMask = kOffScale + (kTcQ + kTcK) * 4;  // additive mask per key of the tile
-constexpr int kOffBar = kOffMask + kTcK * 4;
-constexpr int kTcSmem = kOffBar + 64 + 1024 /*align slack*/;
-constexpr uint32_t kTcTmemCols = 256;
-constexpr int kTmemPh = 0;        // P hi (after the scores are consumed)
-constexpr int kTmemPl = kTcK;     // P lo
-constexpr int kTmemO = 2 * kTcK;  // O_tile
-static_assert(2 * kTcSmem <= 227 * 1024, "two CTAs per SM");
+constexpr int kQAtom = kTcQ * 128;  // one 128-byte-wide column block of 128 rows
+
+// Tiling of the tensor-core attention: KT keys per tile, NW warps per CTA
+// (NW / 4 warps share each TMEM lane quadrant, i.e. each query row).
+//   <64, 8>: 84 KB shared memory, 256 TMEM columns, two CTAs per SM;
+//   <32, 4>: 58 KB, 128 TMEM columns, three CTAs per SM (every CTA of a
+//            batch-32 DistilBERT layer resident at once), one warp per row
+//            block (no cross-warp row max / sum exchange).
+template <int KT, int NW>
+struct AttTc {
+  static constexpr int kThreads = 32 * NW;
+  static constexpr int kWPQ = NW / 4;          // warps per lane quadrant
+  static constexpr int kSC = KT / kWPQ;        // score columns per thread
+  static constexpr int kOC = 64 / kWPQ;        // context columns per thread
+  static constexpr int kQLoads = 2048 / kThreads;       // float4 of Q per thread
+  static constexpr int kKLoads = KT * 16 / kThreads;    // float4 of K per thread per tile
+  static constexpr int kKAtom = KT * 128;      // K slices: KT rows x 128 B per block
+  static constexpr int kVAtom = 64 * 128;      // V^T: 64 rows (d) x 32 keys (128 B) per block
+  static constexpr int kVBlocks = KT / 32;
+  static constexpr int kOffQs = 0;                            // Q slices: 2 blocks (0|1, 2|3)
+  static constexpr int kOffKs = kOffQs + 2 * kQAtom;          // K slices: 2 blocks
+  static constexpr int kOffVh = kOffKs + 2 * kKAtom;          // V^T hi / lo
+  static constexpr int kOffVl = kOffVh + kVBlocks * kVAtom;
+  static constexpr int kOffRed = kOffVl + kVBlocks * kVAtom;  // row max / sum exchange
+  static constexpr int kRedFloats = 2 * kWPQ * kTcQ > 32 ? 2 * kWPQ * kTcQ : 32;
+  static constexpr int kOffScale = kOffRed + kRedFloats * 4;  // 2^(nq-1) per row, 2^(nk-1) per key
+  static constexpr int kOffMask = kOffScale + (kTcQ + KT) * 4;  // additive mask of the tile
+  static constexpr int kOffBar = kOffMask + KT * 4;
+  static constexpr int kSmem = kOffBar + 64 + 1024 /*align slack*/;
+  static constexpr uint32_t kTmemCols = 4 * KT;  // the score levels; P and O_tile reuse them
+  static constexpr int kTmemPh = 0;              // P hi (after the scores are consumed)
+  static constexpr int kTmemPl = KT;             // P lo
+  static constexpr int kTmemO = 2 * KT;          // O_tile (64 columns)
+  static constexpr int kMinBlocks = NW == 8 ? 2 : 3;
+  static_assert(kTmemO + 64 <= (int)kTmemCols, "TMEM layout");
+  static_assert(kMinBlocks * kSmem <= 227 * 1024, "CTAs per SM");
+  static_assert(kSC % 16 == 0 && kOC % 16 == 0, "16-column TMEM accesses");
+};
 
 // The value of x, hidden from the optimiser (no hoisting of what depends on it).
 __device__ __forceinline__ uint32_t opaque_u32(uint32_t x) {
@@ -315,27 +334,29 @@ __device__ __forceinline__ float slice_row_store(uint8_t* base, int block, int r
   return pow2f(n - 1);
 }
 
-template <bool C_POW2>
-__global__ void __launch_bounds__(kTcThreads, 2)
+template <int KT, int NW, bool C_POW2>
+__global__ void __launch_bounds__(32 * NW, (NW == 8 ? 2 : 3))
     attention_tc_kernel(const float* __restrict__ q, const float* __restrict__ k,
                         const float* __restrict__ v, int ld, float* __restrict__ out, int H, int S,
                         int nh, float c, const float* __restrict__ mask, int mask_per_batch,
                         float2* __restrict__ minmax) {
+  using A = AttTc<KT, NW>;
   extern __shared__ __align__(1024) uint8_t att_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(att_raw) + 1023) & ~uintptr_t(1023));
-  float* red_max = reinterpret_cast<float*>(sm + kOffRed);
-  float* red_sum = red_max + 2 * kTcQ;
-  float* q_scale = reinterpret_cast<float*>(sm + kOffScale);
+  float* red_max = reinterpret_cast<float*>(sm + A::kOffRed);
+  float* red_sum = red_max + A::kWPQ * kTcQ;
+  float* q_scale = reinterpret_cast<float*>(sm + A::kOffScale);
   float* k_scale = q_scale + kTcQ;
-  float* m_tile = reinterpret_cast<float*>(sm + kOffMask);
-  uint64_t* bar_s = reinterpret_cast<uint64_t*>(sm + kOffBar);
+  float* m_tile = reinterpret_cast<float*>(sm + A::kOffMask);
+  uint64_t* bar_s = reinterpret_cast<uint64_t*>(sm + A::kOffBar);
   uint64_t* bar_o = bar_s + 1;
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bar_s + 2);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int quad = warp & 3, cg = warp >> 2;
   const int row = quad * 32 + lane;  // query row within the tile = TMEM lane
-  const int col0 = cg * kTcCols;     // first score / context column of this thread
+  const int scol0 = cg * A::kSC;     // first score column of this thread
+  const int ocol0 = cg * A::kOC;     // first context column of this thread
   const int bh = blockIdx.y;
   const int b = bh / nh, h = bh % nh;
   const int q0 = blockIdx.x * kTcQ;
@@ -345,6 +366,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
   // Q / K rows: 16 threads per 256-byte row; V: thread = column d (tid % 64)
   // of keys 16 (tid / 64) .. +15, stored as row d of V^T
   const int kv_row = tid >> 4, kv_col = (tid & 15) * 4;
+  constexpr int kRowStep = A::kThreads / 16;  // rows between a thread's Q / K loads
   const int v_d = tid & 63, v_key = (tid >> 6) * 16;
 
   if (tid == 0) {
@@ -353,40 +375,40 @@ __global__ void __launch_bounds__(kTcThreads, 2)
     fence_barrier_init();
   }
   if (warp == 0) {
-    tmem_alloc(tslot, kTcTmemCols);
+    tmem_alloc(tslot, A::kTmemCols);
     tmem_relinquish();
   }
   // barrier init and TMEM allocation overlap the previous kernel; q / k / v
   // (its outputs) are read only from here on
   pdl_wait();
   pdl_trigger();
-  float4 nk[4];
+  float4 nk[A::kKLoads];
   float nm = 0.0f;  // the tile's additive mask value for key tid (tid < 64)
   auto load_k = [&](int k0) {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int kr = k0 + kv_row + 16 * i;
+    for (int i = 0; i < A::kKLoads; ++i) {
+      const int kr = k0 + kv_row + kRowStep * i;
       nk[i] = kr < S ? __ldg(reinterpret_cast<const float4*>(k + head + (size_t)kr * ld + kv_col))
                      : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    if (tid < kTcK) {
+    if (tid < KT) {
       const int key = k0 + tid;
       nm = key >= S ? -INFINITY : (mrow ? __ldg(mrow + key) : 0.0f);
     }
   };
   {
-    float4 vq[8];
+    float4 vq[A::kQLoads];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int r = (i * kTcThreads + tid) >> 4, qi = q0 + r;
+    for (int i = 0; i < A::kQLoads; ++i) {
+      const int r = kv_row + kRowStep * i, qi = q0 + r;
       vq[i] = qi < S ? __ldg(reinterpret_cast<const float4*>(q + head + (size_t)qi * ld + kv_col))
                      : make_float4(0.f, 0.f, 0.f, 0.f);
     }
     load_k(0);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int r = (i * kTcThreads + tid) >> 4;
-      const float f = slice_row_store(sm + kOffQs, kQAtom, r, kv_col, vq[i]);
+    for (int i = 0; i < A::kQLoads; ++i) {
+      const int r = kv_row + kRowStep * i;
+      const float f = slice_row_store(sm + A::kOffQs, kQAtom, r, kv_col, vq[i]);
       if (kv_col == 0) q_scale[r] = f;
     }
   }
@@ -400,19 +422,19 @@ __global__ void __launch_bounds__(kTcThreads, 2)
   const float qsc = q_scale[row];
   const float qf = __fmul_rn(qsc, inv_c);  // a power of two when c is
 
-  float m_run = -INFINITY, l_part = 0.0f, o[kTcCols];
+  float m_run = -INFINITY, l_part = 0.0f, o[A::kOC];
 #pragma unroll
-  for (int d = 0; d < kTcCols; ++d) o[d] = 0.0f;
+  for (int d = 0; d < A::kOC; ++d) o[d] = 0.0f;
   bool ok = true;
   uint32_t phase = 0;
-  for (int k0 = 0; k0 < S; k0 += kTcK, phase ^= 1) {
+  for (int k0 = 0; k0 < S; k0 += KT, phase ^= 1) {
     // 1. K slices and the mask of this tile
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float f = slice_row_store(sm + kOffKs, kKAtom, kv_row + 16 * i, kv_col, nk[i]);
-      if (kv_col == 0) k_scale[kv_row + 16 * i] = f;
+    for (int i = 0; i < A::kKLoads; ++i) {
+      const float f = slice_row_store(sm + A::kOffKs, A::kKAtom, kv_row + kRowStep * i, kv_col, nk[i]);
+      if (kv_col == 0) k_scale[kv_row + kRowStep * i] = f;
     }
-    if (tid < kTcK) m_tile[tid] = nm;
+    if (tid < KT) m_tile[tid] = nm;
     fence_proxy_async_smem();
     tc_fence_before();
     ok = __syncthreads_and(ok) != 0;
@@ -422,7 +444,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
       tc_fence_after();
       // the operand addresses are made opaque here so the compiler does not
       // hoist 40 loop-invariant descriptors into registers for the whole loop
-      const uint32_t a_qs = opaque_u32(a_sm + kOffQs), a_ks = opaque_u32(a_sm + kOffKs);
+      const uint32_t a_qs = opaque_u32(a_sm + A::kOffQs), a_ks = opaque_u32(a_sm + A::kOffKs);
 #pragma unroll
       for (int L = 0; L < 4; ++L) {
 #pragma unroll
@@ -433,9 +455,9 @@ __global__ void __launch_bounds__(kTcThreads, 2)
             // slice i of Q / slice j of K, d half hd (32 bytes each); the
             // most significant slice is signed, the others unsigned
             const uint32_t ao = (i >> 1) * kQAtom + (i & 1) * 64 + hd * 32;
-            const uint32_t bo = (j >> 1) * kKAtom + (j & 1) * 64 + hd * 32;
-            mma_i8(tmem_base + (uint32_t)(L * kTcK), smem_desc_k128(a_qs + ao),
-                   smem_desc_k128(a_ks + bo), idesc_i8(kTcQ, kTcK, i == 0, j == 0), (i | hd) != 0);
+            const uint32_t bo = (j >> 1) * A::kKAtom + (j & 1) * 64 + hd * 32;
+            mma_i8(tmem_base + (uint32_t)(L * KT), smem_desc_k128(a_qs + ao),
+                   smem_desc_k128(a_ks + bo), idesc_i8(kTcQ, KT, i == 0, j == 0), (i | hd) != 0);
           }
         }
       }
@@ -455,7 +477,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
       }
 #pragma unroll
       for (int g = 0; g < 4; ++g)
-        split_store(sm + kOffVh, sm + kOffVl, kKAtom, v_d, v_key + 4 * g, nv[g]);
+        split_store(sm + A::kOffVh, sm + A::kOffVl, A::kVAtom, v_d, v_key + 4 * g, nv[g]);
     }
     ok = mbar_wait_warp(bar_s, phase, ICX_DEVICE_TIMEOUT_EPILOGUE);
     tc_fence_after();
@@ -463,8 +485,8 @@ __global__ void __launch_bounds__(kTcThreads, 2)
     // rounding per step, then 2^(nq-1) 2^(nk-1), Div(c), Add(mask)
     float pmax = -INFINITY;
 #pragma unroll
-    for (int hcol = 0; hcol < kTcCols; hcol += 16) {
-      const uint32_t t = t_lane + (uint32_t)(col0 + hcol);
+    for (int hcol = 0; hcol < A::kSC; hcol += 16) {
+      const uint32_t t = t_lane + (uint32_t)(scol0 + hcol);
       float f[16];
       uint32_t sc[16];
       // one level at a time (16 registers in flight)
@@ -472,7 +494,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
       for (int L = 3; L >= 0; --L) {
         uint32_t r[16];
         if (ok) {
-          tmem_ld_32x32b_x16(t + (uint32_t)(L * kTcK), r);
+          tmem_ld_32x32b_x16(t + (uint32_t)(L * KT), r);
           tmem_ld_wait_regs16(r);
         }
 #pragma unroll
@@ -487,7 +509,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         const float g = f[j];
-        const int jj = col0 + hcol + j;
+        const int jj = scol0 + hcol + j;
         float t2 = C_POW2 ? __fmul_rn(__fmul_rn(g, qf), k_scale[jj])  // exact: powers of two
                           : __fdiv_rn(__fmul_rn(__fmul_rn(g, qsc), k_scale[jj]), c);
         t2 = __fadd_rn(t2, m_tile[jj]);  // -inf past S
@@ -499,21 +521,28 @@ __global__ void __launch_bounds__(kTcThreads, 2)
       tmem_st_32x32b_x16(t, sc);
     }
     tmem_st_wait();
-    red_max[cg * kTcQ + row] = pmax;
-    tc_fence_before();
-    ok = __syncthreads_and(ok) != 0;  // every score column has been read
-    if (!ok) break;
-    tc_fence_after();
-    const float tmax = fmaxf(red_max[row], red_max[kTcQ + row]);
+    float tmax = pmax;
+    if (A::kWPQ > 1) {
+      // the row max over the warps sharing the row; also: every score
+      // column has been read before any P overwrites it
+      red_max[cg * kTcQ + row] = pmax;
+      tc_fence_before();
+      ok = __syncthreads_and(ok) != 0;
+      if (!ok) break;
+      tc_fence_after();
+      tmax = red_max[row];
+#pragma unroll
+      for (int w = 1; w < A::kWPQ; ++w) tmax = fmaxf(tmax, red_max[w * kTcQ + row]);
+    }
     // online softmax: exp(a - m) = 2^(a*log2e - m*log2e)
     const float m_new = fmaxf(m_run, tmax);
     const float ml = m_new == -INFINITY ? 0.0f : m_new * kLog2e;  // a fully masked row stays 0
     const float alpha = m_run == -INFINITY ? 0.0f : ex2f(fmaf(m_run, kLog2e, -ml));
     float rsum = 0.0f;
 #pragma unroll
-    for (int hcol = 0; hcol < kTcCols; hcol += 16) {
+    for (int hcol = 0; hcol < A::kSC; hcol += 16) {
       uint32_t hi[16], lo[16], sc[16];
-      tmem_ld_32x32b_x16(t_lane + (uint32_t)(col0 + hcol), sc);
+      tmem_ld_32x32b_x16(t_lane + (uint32_t)(scol0 + hcol), sc);
       tmem_ld_wait_regs16(sc);
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
@@ -523,8 +552,8 @@ __global__ void __launch_bounds__(kTcThreads, 2)
         hi[j] = __float_as_uint(eh);
         lo[j] = __float_as_uint(tf32_round(__fsub_rn(e, eh)));
       }
-      tmem_st_32x32b_x16(t_lane + (uint32_t)(kTmemPh + col0 + hcol), hi);
-      tmem_st_32x32b_x16(t_lane + (uint32_t)(kTmemPl + col0 + hcol), lo);
+      tmem_st_32x32b_x16(t_lane + (uint32_t)(A::kTmemPh + scol0 + hcol), hi);
+      tmem_st_32x32b_x16(t_lane + (uint32_t)(A::kTmemPl + scol0 + hcol), lo);
     }
     l_part = l_part * alpha + rsum;
     m_run = m_new;
@@ -535,28 +564,28 @@ __global__ void __launch_bounds__(kTcThreads, 2)
     // 4. O_tile = P V; the next K tile meanwhile
     if (tid == 0) {
       tc_fence_after();
-      const uint32_t a_v_h = opaque_u32(a_sm + kOffVh), a_v_l = opaque_u32(a_sm + kOffVl);
+      const uint32_t a_v_h = opaque_u32(a_sm + A::kOffVh), a_v_l = opaque_u32(a_sm + A::kOffVl);
 #pragma unroll
-      for (int j = 0; j < kTcK / 8; ++j) {
+      for (int j = 0; j < KT / 8; ++j) {
         // k-step j = keys 8j..8j+7: P columns 8j.., V^T column block j/4
-        const uint32_t bo = (j >> 2) * kKAtom + (j & 3) * 32;
+        const uint32_t bo = (j >> 2) * A::kVAtom + (j & 3) * 32;
         const uint64_t vh = smem_desc_k128(a_v_h + bo), vl = smem_desc_k128(a_v_l + bo);
-        const uint32_t ph = tmem_base + (uint32_t)(kTmemPh + 8 * j);
-        const uint32_t pl = tmem_base + (uint32_t)(kTmemPl + 8 * j);
-        mma_tf32_ts(tmem_base + kTmemO, ph, vh, idesc_o, j > 0);
-        mma_tf32_ts(tmem_base + kTmemO, ph, vl, idesc_o, true);
-        mma_tf32_ts(tmem_base + kTmemO, pl, vh, idesc_o, true);
+        const uint32_t ph = tmem_base + (uint32_t)(A::kTmemPh + 8 * j);
+        const uint32_t pl = tmem_base + (uint32_t)(A::kTmemPl + 8 * j);
+        mma_tf32_ts(tmem_base + A::kTmemO, ph, vh, idesc_o, j > 0);
+        mma_tf32_ts(tmem_base + A::kTmemO, ph, vl, idesc_o, true);
+        mma_tf32_ts(tmem_base + A::kTmemO, pl, vh, idesc_o, true);
       }
       mma_commit(bar_o);
     }
-    if (k0 + kTcK < S) load_k(k0 + kTcK);
+    if (k0 + KT < S) load_k(k0 + KT);
     ok = mbar_wait_warp(bar_o, phase, ICX_DEVICE_TIMEOUT_EPILOGUE);
     tc_fence_after();
     if (ok) {
 #pragma unroll
-      for (int hcol = 0; hcol < kTcCols; hcol += 16) {
+      for (int hcol = 0; hcol < A::kOC; hcol += 16) {
         uint32_t r[16];
-        tmem_ld_32x32b_x16(t_lane + (uint32_t)(kTmemO + col0 + hcol), r);
+        tmem_ld_32x32b_x16(t_lane + (uint32_t)(A::kTmemO + ocol0 + hcol), r);
         tmem_ld_wait_regs16(r);
 #pragma unroll
         for (int d = 0; d < 16; ++d) o[hcol + d] = fmaf(o[hcol + d], alpha, __uint_as_float(r[d]));
@@ -570,10 +599,13 @@ __global__ void __launch_bounds__(kTcThreads, 2)
   const int qi = q0 + row;
   float mn = 0.0f, mx = 0.0f;  // (min, max) of what this CTA writes, seeded like DynamicQuantizeLinear
   if (ok && qi < S) {
-    const float inv = 1.0f / (red_sum[row] + red_sum[kTcQ + row]);
-    float4* orow = reinterpret_cast<float4*>(out + ((size_t)b * S + qi) * H + (size_t)h * kAttDh + col0);
+    float l = red_sum[row];
 #pragma unroll
-    for (int d = 0; d < kTcCols; d += 4) {
+    for (int w = 1; w < A::kWPQ; ++w) l += red_sum[w * kTcQ + row];
+    const float inv = 1.0f / l;
+    float4* orow = reinterpret_cast<float4*>(out + ((size_t)b * S + qi) * H + (size_t)h * kAttDh + ocol0);
+#pragma unroll
+    for (int d = 0; d < A::kOC; d += 4) {
       const float4 w = make_float4(o[d] * inv, o[d + 1] * inv, o[d + 2] * inv, o[d + 3] * inv);
       orow[d / 4] = w;
       mn = fminf(fminf(mn, fminf(w.x, w.y)), fminf(w.z, w.w));
@@ -589,13 +621,13 @@ __global__ void __launch_bounds__(kTcThreads, 2)
     }
     if (lane == 0) {
       red_max[warp] = mn;  // the row max / sum areas are free now
-      red_max[8 + warp] = mx;
+      red_max[16 + warp] = mx;
     }
     __syncthreads();
     if (tid == 0) {
-      for (int w = 1; w < kTcThreads / 32; ++w) {
+      for (int w = 1; w < A::kThreads / 32; ++w) {
         mn = fminf(mn, red_max[w]);
-        mx = fmaxf(mx, red_max[8 + w]);
+        mx = fmaxf(mx, red_max[16 + w]);
       }
       minmax[blockIdx.y * gridDim.x + blockIdx.x] = make_float2(mn, mx);
     }
@@ -604,7 +636,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
   __syncthreads();
   if (warp == 0) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, kTcTmemCols);
+    tmem_dealloc(tmem_base, A::kTmemCols);
   }
 }
 
@@ -638,11 +670,25 @@ int launch_attention_f32(cudaStream_t s, const float* q, const float* k, const f
                 "Attention: %d (min, max) partials exceed %d", parts, ICX_MAX_MINMAX_PARTIALS);
     int cexp;
     const bool c_pow2 = frexpf(c, &cexp) == 0.5f;
-    auto kern = c_pow2 ? attention_tc_kernel<true> : attention_tc_kernel<false>;
-    ICX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem));
+    static const bool wide = [] {  // the <64, 8> tiling instead of <32, 4>
+      const char* e = getenv("ICONNX_ATTENTION_TILE");
+      return e != nullptr && strcmp(e, "64") == 0;
+    }();
     dim3 grid((unsigned)((S + kTcQ - 1) / kTcQ), (unsigned)(B * nh));
-    launch_pdl(kern, dim3(grid), dim3(kTcThreads), kTcSmem, s, q, k, v, (int)ld, out, (int)H, (int)S, (int)nh, c, mask,
-                                           mask_per_batch ? 1 : 0, reinterpret_cast<float2*>(minmax));
+    auto launch = [&](auto kern, int threads, int smem) -> int {
+      ICX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+      launch_pdl(kern, grid, dim3(threads), smem, s, q, k, v, (int)ld, out, (int)H, (int)S, (int)nh,
+                 c, mask, mask_per_batch ? 1 : 0, reinterpret_cast<float2*>(minmax));
+      return ICX_OK;
+    };
+    int rc;
+    if (wide)
+      rc = c_pow2 ? launch(attention_tc_kernel<64, 8, true>, 256, AttTc<64, 8>::kSmem)
+                  : launch(attention_tc_kernel<64, 8, false>, 256, AttTc<64, 8>::kSmem);
+    else
+      rc = c_pow2 ? launch(attention_tc_kernel<32, 4, true>, 128, AttTc<32, 4>::kSmem)
+                  : launch(attention_tc_kernel<32, 4, false>, 128, AttTc<32, 4>::kSmem);
+    if (rc) return rc;
     ICX_LAUNCH_CHECK();
     if (n_minmax) *n_minmax = parts;
     return ICX_OK;
