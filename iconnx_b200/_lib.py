@@ -43,6 +43,8 @@ PROTOTYPES = {
     "icx_engine_add_initializer": (_i, [_vp, ctypes.c_char_p, _i, _i, _vp, _vp]),
     "icx_engine_add_node": (_i, [_vp, ctypes.c_char_p, ctypes.c_char_p, _i, _vp, _i, _vp, _i, _vp]),
     "icx_engine_run": (_i, [_vp, _i, _vp, _vp, _vp, _vp, _vp, _i, _vp]),
+    "icx_engine_submit": (_i, [_vp, _i, _vp, _vp, _vp, _vp, _vp, _i, _vp, _vp, _vp, _vp]),
+    "icx_engine_wait": (_i, [_vp, ctypes.c_int64]),
     "icx_engine_output_info": (_i, [_vp, ctypes.c_char_p, _vp, _vp, _vp]),
     "icx_engine_output_copy": (_i, [_vp, ctypes.c_char_p, _vp, _sz]),
     "icx_engine_plan": (ctypes.c_char_p, [_vp]),

@@ -212,9 +212,11 @@ class Engine {
     return ICX_OK;
   }
 
-  int run(const std::vector<std::string>& names, const std::vector<int>& dtypes,
-          const std::vector<Shape>& shapes, const std::vector<const void*>& host,
-          const std::vector<std::string>& outputs) {
+  // Validates the inputs, (re)compiles when their shapes or the requested
+  // outputs change, and queues the inputs' host->device copies on the stream.
+  int stage_inputs(const std::vector<std::string>& names, const std::vector<int>& dtypes,
+                   const std::vector<Shape>& shapes, const std::vector<const void*>& host,
+                   const std::vector<std::string>& outputs) {
     ICX_CUDA(cudaSetDevice(device_));
     // input-shape guard (src/cuda/inference/mod.rs:441-460): declared
     // static dimensions must match; dynamic ones (<= 0) may vary.
@@ -258,9 +260,21 @@ class Engine {
       const size_t bytes = (size_t)numel(v.shape) * dtype_size(v.dtype);
       if (bytes) ICX_CUDA(cudaMemcpyAsync(v.ptr, host[i], bytes, cudaMemcpyHostToDevice, stream_));
     }
-    int rc = execute();
+    return ICX_OK;
+  }
+
+  int run(const std::vector<std::string>& names, const std::vector<int>& dtypes,
+          const std::vector<Shape>& shapes, const std::vector<const void*>& host,
+          const std::vector<std::string>& outputs) {
+    int rc = stage_inputs(names, dtypes, shapes, host, outputs);
+    if (rc) return rc;
+    rc = execute();
     if (rc) return rc;
     ICX_CUDA(cudaStreamSynchronize(stream_));
+    return check_err_flag();
+  }
+
+  int check_err_flag() {
     if (err_flag_) {
       int e = 0;
       ICX_CUDA(cudaMemcpy(&e, err_flag_, sizeof(int), cudaMemcpyDeviceToHost));
@@ -299,6 +313,71 @@ class Engine {
       ICX_CUDA(cudaStreamSynchronize(stream_));
     }
     return ICX_OK;
+  }
+
+  // Pipelined run (a serving loop): stage the inputs, run the plan, snapshot
+  // the requested outputs into one of two device staging sets on the compute
+  // stream, and download them into the caller's host buffers on a second
+  // stream, so the download of one submission overlaps the next one's
+  // compute.  The host buffers (ideally pinned) must stay valid until
+  // wait(ticket) returns; a staging set is reused only after its download
+  // has completed.
+  int submit(const std::vector<std::string>& names, const std::vector<int>& dtypes,
+             const std::vector<Shape>& shapes, const std::vector<const void*>& host,
+             const std::vector<std::string>& outputs, const std::vector<void*>& host_out,
+             const std::vector<size_t>& out_bytes, int64_t* ticket) {
+    int rc = stage_inputs(names, dtypes, shapes, host, outputs);
+    if (rc) return rc;
+    rc = execute();
+    if (rc) return rc;
+    if (!copy_stream_) ICX_CUDA(cudaStreamCreateWithFlags(&copy_stream_, cudaStreamNonBlocking));
+    Pending& p = pend_[next_ticket_ & 1];
+    if (!p.ready) {
+      ICX_CUDA(cudaEventCreateWithFlags(&p.ready, cudaEventDisableTiming));
+      ICX_CUDA(cudaEventCreateWithFlags(&p.done, cudaEventDisableTiming));
+    }
+    if (p.busy) ICX_CUDA(cudaStreamWaitEvent(stream_, p.done, 0));  // its last download is done
+    if (p.buf.size() < outputs.size()) {
+      p.buf.resize(outputs.size(), nullptr);
+      p.cap.resize(outputs.size(), 0);
+    }
+    std::vector<size_t> need(outputs.size());
+    for (size_t k = 0; k < outputs.size(); ++k) {
+      const Val& v = vals_[outputs[k]];
+      need[k] = (size_t)numel(v.shape) * dtype_size(v.dtype);
+      ICX_REQUIRE(out_bytes[k] >= need[k], "submit: output '%s' buffer %zu < %zu bytes",
+                  outputs[k].c_str(), out_bytes[k], need[k]);
+      if (p.cap[k] < need[k]) {
+        ICX_CUDA(cudaStreamSynchronize(stream_));
+        if (p.buf[k]) ICX_CUDA(cudaFree(p.buf[k]));
+        ICX_CUDA(cudaMalloc(&p.buf[k], need[k]));
+        p.cap[k] = need[k];
+      }
+      if (need[k])
+        ICX_CUDA(cudaMemcpyAsync(p.buf[k], resolve(outputs[k]), need[k], cudaMemcpyDeviceToDevice, stream_));
+    }
+    ICX_CUDA(cudaEventRecord(p.ready, stream_));
+    ICX_CUDA(cudaStreamWaitEvent(copy_stream_, p.ready, 0));
+    for (size_t k = 0; k < outputs.size(); ++k)
+      if (need[k])
+        ICX_CUDA(cudaMemcpyAsync(host_out[k], p.buf[k], need[k], cudaMemcpyDeviceToHost, copy_stream_));
+    ICX_CUDA(cudaEventRecord(p.done, copy_stream_));
+    p.busy = true;
+    p.ticket = next_ticket_;
+    *ticket = next_ticket_++;
+    return ICX_OK;
+  }
+
+  // Blocks until submission `ticket` has its outputs in the host buffers.
+  int wait(int64_t ticket) {
+    ICX_REQUIRE(ticket >= 0 && ticket < next_ticket_, "wait: unknown ticket %lld", (long long)ticket);
+    Pending& p = pend_[ticket & 1];
+    if (p.busy && p.ticket == ticket) {
+      ICX_CUDA(cudaEventSynchronize(p.done));
+      p.busy = false;
+    }
+    // an older ticket of this slot completed before the slot was reused
+    return check_err_flag();
   }
 
   // Human-readable plan: one line per step ("op node -> out").
@@ -407,6 +486,12 @@ class Engine {
     for (void* p : scratch_) cudaFree(p);
     if (blas_) cublasDestroy(blas_);
     if (blas_ws_) cudaFree(blas_ws_);
+    for (auto& p : pend_) {
+      for (void* b : p.buf) if (b) cudaFree(b);
+      if (p.ready) cudaEventDestroy(p.ready);
+      if (p.done) cudaEventDestroy(p.done);
+    }
+    if (copy_stream_) cudaStreamDestroy(copy_stream_);
     if (stream_) cudaStreamDestroy(stream_);
   }
 
@@ -1723,6 +1808,17 @@ class Engine {
   std::map<int, FusedAttn> attn_;
   std::set<int> skip_;
   std::set<std::string> folded_;  // initializers derived at compile (folded / converted)
+  // submit / wait: two staging sets of the requested outputs
+  struct Pending {
+    std::vector<void*> buf;
+    std::vector<size_t> cap;
+    cudaEvent_t ready = nullptr, done = nullptr;
+    bool busy = false;
+    int64_t ticket = -1;
+  };
+  Pending pend_[2];
+  cudaStream_t copy_stream_ = nullptr;
+  int64_t next_ticket_ = 0;
   std::map<int, int> dql_mode_;
   int n_slots_ = 0;
   std::vector<int> minmax_count_;
@@ -1819,6 +1915,41 @@ extern "C" int icx_engine_run(icx_engine* h, int n_in, const char* const* names,
   for (int i = 0; i < n_out; ++i) outs.push_back(outputs[i]);
   h->e->set_pending_outputs(outs);
   return h->e->run(nm, dt, sh, hp, outs);
+}
+
+extern "C" int icx_engine_submit(icx_engine* h, int n_in, const char* const* names,
+                                 const int* dtypes, const int* ranks, const int64_t* dims,
+                                 const void* const* host, int n_out, const char* const* outputs,
+                                 void* const* host_out, const size_t* host_out_bytes,
+                                 int64_t* ticket) {
+  ICX_REQUIRE(h && n_in >= 0 && n_out >= 0 && ticket && (n_out == 0 || (host_out && host_out_bytes)),
+              "submit: bad arguments");
+  std::vector<std::string> nm, outs;
+  std::vector<int> dt;
+  std::vector<std::vector<int64_t>> sh;
+  std::vector<const void*> hp;
+  size_t off = 0;
+  for (int i = 0; i < n_in; ++i) {
+    nm.push_back(names[i]);
+    dt.push_back(dtypes[i]);
+    sh.emplace_back(dims + off, dims + off + ranks[i]);
+    off += (size_t)ranks[i];
+    hp.push_back(host[i]);
+  }
+  std::vector<void*> ho;
+  std::vector<size_t> hb;
+  for (int i = 0; i < n_out; ++i) {
+    outs.push_back(outputs[i]);
+    ho.push_back(host_out[i]);
+    hb.push_back(host_out_bytes[i]);
+  }
+  h->e->set_pending_outputs(outs);
+  return h->e->submit(nm, dt, sh, hp, outs, ho, hb, ticket);
+}
+
+extern "C" int icx_engine_wait(icx_engine* h, int64_t ticket) {
+  ICX_REQUIRE(h, "wait: null engine");
+  return h->e->wait(ticket);
 }
 
 extern "C" int icx_engine_output_info(icx_engine* h, const char* name, int* dtype, int* rank,

@@ -146,6 +146,41 @@ class GpuGraphExecutor:
         check(self._L.icx_engine_run(self._h, k, _strs(names), dtypes, ranks, dims, ptrs,
                                      len(outputs), _strs(list(outputs))))
 
+    def submit(self, inputs: dict, outputs, host_outs) -> int:
+        """Pipelined run for serving loops: queues the inputs' upload, the
+        plan and the download of ``outputs`` into the preallocated arrays
+        ``host_outs`` (pinned memory lets the download overlap the next
+        submission's compute) and returns a ticket without waiting.  The
+        input and output arrays must stay alive until :meth:`wait`.  Two
+        submissions can be in flight."""
+        names = list(inputs)
+        arrs = [np.ascontiguousarray(inputs[n]) for n in names]
+        for n, a in zip(names, arrs):
+            if a.dtype not in _NP2ICX:
+                raise IcxError(-1, f"submit: input '{n}' dtype {a.dtype} unsupported")
+        outs = list(outputs)
+        if len(host_outs) != len(outs) or any(not h.flags.c_contiguous for h in host_outs):
+            raise IcxError(-1, "submit: one contiguous host array per output")
+        k = len(names)
+        dtypes = (ctypes.c_int * max(k, 1))(*[_NP2ICX[a.dtype] for a in arrs])
+        ranks = (ctypes.c_int * max(k, 1))(*[a.ndim for a in arrs])
+        flat = [d for a in arrs for d in a.shape]
+        dims = (ctypes.c_int64 * max(len(flat), 1))(*flat)
+        ptrs = (ctypes.c_void_p * max(k, 1))(*[a.ctypes.data for a in arrs])
+        optrs = (ctypes.c_void_p * max(len(outs), 1))(*[h.ctypes.data for h in host_outs])
+        obytes = (ctypes.c_size_t * max(len(outs), 1))(*[h.nbytes for h in host_outs])
+        ticket = ctypes.c_int64()
+        check(self._L.icx_engine_submit(self._h, k, _strs(names), dtypes, ranks, dims, ptrs,
+                                        len(outs), _strs(outs), optrs, obytes, ctypes.byref(ticket)))
+        self._in_flight = getattr(self, "_in_flight", {})
+        self._in_flight[ticket.value] = (arrs, list(host_outs))
+        return ticket.value
+
+    def wait(self, ticket: int) -> None:
+        """Blocks until submission ``ticket`` has its outputs in its host arrays."""
+        check(self._L.icx_engine_wait(self._h, int(ticket)))
+        getattr(self, "_in_flight", {}).pop(int(ticket), None)
+
     def fetch(self, name: str, out: np.ndarray | None = None) -> np.ndarray:
         dt, rk = ctypes.c_int(), ctypes.c_int()
         dims = (ctypes.c_int64 * 6)()

@@ -255,6 +255,20 @@ ICX_API int icx_engine_run(icx_engine* e, int n_in, const char* const* names, co
 ICX_API int icx_engine_output_info(icx_engine* e, const char* name, int* dtype, int* rank,
                                    int64_t* dims /* [6] */);
 ICX_API int icx_engine_output_copy(icx_engine* e, const char* name, void* host, size_t bytes);
+/* Pipelined run for serving loops (no reference counterpart; the reference's
+ * run is synchronous): queues the inputs' upload, the plan and the download
+ * of the requested outputs into host_out[k] (host_out_bytes[k] bytes each;
+ * pinned memory lets the download overlap the next submission's compute)
+ * and returns a ticket without waiting.  The host buffers of a submission
+ * must stay valid until icx_engine_wait(ticket) returns.  Up to two
+ * submissions are in flight; a third waits on the GPU for the oldest
+ * download. */
+ICX_API int icx_engine_submit(icx_engine* e, int n_in, const char* const* names, const int* dtypes,
+                              const int* ranks, const int64_t* dims, const void* const* host,
+                              int n_out, const char* const* outputs, void* const* host_out,
+                              const size_t* host_out_bytes, int64_t* ticket);
+/* Blocks until submission `ticket` has its outputs in its host buffers. */
+ICX_API int icx_engine_wait(icx_engine* e, int64_t ticket);
 /* The compiled plan, one "op node -> output" line per launch step. */
 ICX_API const char* icx_engine_plan(icx_engine* e);
 /* Replay the compiled plan as a CUDA graph after the first run (default on). */

@@ -224,3 +224,26 @@ def test_quantized_export_through_onnx_file(tmp_path):
     r = cpu.run(inp, list(outs))
     np.testing.assert_array_equal(g[outs[0]].view(np.uint32), r[outs[0]].view(np.uint32))
     np.testing.assert_allclose(g[outs[1]], r[outs[1]], atol=1e-5, rtol=0)
+
+
+@gpu
+def test_submit_wait_pipeline_equals_run():
+    """submit / wait (two submissions in flight, outputs downloaded into host
+    arrays on a second stream) gives exactly what run() gives, per submission,
+    including when a third submission reuses the first one's staging set."""
+    from iconnx_b200.engine import GpuGraphExecutor
+    cfg = graphs.BertConfig(layers=1, vocab=1000, w_scale=graphs.REALISTIC_W_SCALE)
+    ex = GpuGraphExecutor.new()
+    out = graphs.build_bert(ex, cfg, 2, 16)
+    batches = [graphs.bert_inputs(2, 16, vocab=1000, seed=s) for s in (3, 4, 5, 6)]
+    ref = [ex.run(b, [out])[out].copy() for b in batches]
+    hosts = [np.empty_like(ref[0]) for _ in batches]
+    tickets = []
+    for b, h in zip(batches, hosts):
+        tickets.append(ex.submit(b, [out], [h]))
+        if len(tickets) == 2:
+            ex.wait(tickets.pop(0))
+    for t in tickets:
+        ex.wait(t)
+    for h, r in zip(hosts, ref):
+        np.testing.assert_array_equal(h.view(np.uint32), r.view(np.uint32))
