@@ -1,22 +1,29 @@
-// Fused fp32 attention for the engine's attention fusion: for each
-// (batch, head) and 64-query tile,
+// Fused attention for the engine's attention fusion: for each (batch, head)
+// and query tile,
 //     ctx = softmax(Q K^T / c + mask) V
-// in one kernel, with online (running max / running sum) softmax over
-// 64-key tiles, so the [B, heads, S, S] score tensor never reaches HBM.
-// It replaces the MatMul -> Div -> Add -> Softmax -> MatMul sequence the
-// reference runs as cuBLAS SGEMMs and NVRTC kernels (src/cuda/matmul.rs,
-// src/cuda/reduction.rs).  Arithmetic is fp32 throughout, like the
-// reference: Div by c and Add of the mask are each rounded as the separate
-// ops round them; the softmax normalisation order differs (online), within
-// fp32 rounding.
+// in one kernel, with online (running max / running sum) softmax over key
+// tiles, so the [B, heads, S, S] score tensor never reaches HBM.  It replaces
+// the MatMul -> Div -> Add -> Softmax -> MatMul sequence the reference runs
+// as cuBLAS SGEMMs and NVRTC kernels (src/cuda/matmul.rs,
+// src/cuda/reduction.rs).  Semantics are the reference's fp32: Div by c and
+// Add of the mask are each rounded as the separate ops round them; the
+// softmax normalisation order differs (online), within fp32 rounding.
+//
+// Two kernels:
+//   attention_tc_kernel   the one the engine runs: scores on the int8 tensor
+//                         cores with exact integer accumulation, P V on the
+//                         tf32 tensor cores in split precision (see below);
+//   attention_f32_kernel  CUDA-core fp32 (ICONNX_ATTENTION=simt), kept for
+//                         comparison.
 //
 // Layout: q / k / v rows are `ld` floats apart (the merged QKV GEMM output
 // has ld = 3H), head h occupies columns [h*dh, (h+1)*dh); ctx is [B, S, H].
-// Tiles: 128 threads; thread (ty, tx) = (tid / 16, tid % 16) owns score
-// rows ty + 8 i (i < 8) and key columns tx + 16 j (j < 4), and context
-// columns 4 tx .. 4 tx + 3 of the same rows: 12 shared 16-byte loads per
-// 128 FMAs.  Shared rows are padded to 68 floats so the strided column
-// pattern is bank-conflict free.
+//
+// attention_f32_kernel tiles: 128 threads; thread (ty, tx) = (tid / 16,
+// tid % 16) owns score rows ty + 8 i (i < 8) and key columns tx + 16 j
+// (j < 4), and context columns 4 tx .. 4 tx + 3 of the same rows: 12 shared
+// 16-byte loads per 128 FMAs.  Shared rows are padded to 68 floats so the
+// strided column pattern is bank-conflict free.
 #include "capi.cuh"
 #include "common.cuh"
 #include "glue.h"

@@ -281,37 +281,12 @@ __device__ __forceinline__ uint64_t smem_desc_k128(uint32_t saddr) {
   return d;
 }
 
-// General 128-byte-swizzle descriptor with explicit leading / stride byte
-// offsets.  For an MN-major operand (rows of 128 bytes along M or N, one row
-// per K index) LBO is the distance between 128-byte column blocks along MN
-// and SBO the distance between 8-row groups along K.
-__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
-  uint64_t d = 0;
-  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
-  d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
-  d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
-  d |= (uint64_t)1 << 46;
-  d |= (uint64_t)2 << 61;
-  return d;
-}
-
 // Instruction descriptor for kind::tf32 with an f32 accumulator.  Bits:
 // [4,6) D format (1 = f32), [7,10) / [10,13) A / B format (2 = tf32),
 // [15] A MN-major, [16] B MN-major, [17,23) N>>3, [24,29) M>>4.
 __host__ __device__ constexpr uint32_t idesc_tf32(int M, int N, bool b_mn_major) {
   return (1u << 4) | (2u << 7) | (2u << 10) | ((b_mn_major ? 1u : 0u) << 16) |
          ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
-}
-
-// D[tmem] (+)= A[smem] * B[smem], kind::tf32, one CTA.
-__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
-                                         uint32_t idesc, bool accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"((uint32_t)accumulate)
-      : "memory");
 }
 
 // D[tmem] (+)= A[tmem] * B[smem], kind::tf32: A (M=128 rows = TMEM lanes,
