@@ -102,11 +102,12 @@ constexpr int kStageOutBytes = 32 * 32 * 4;          // one warp's 32x32 output 
 // epilogue (the bottleneck at small K) reads them with broadcast loads.
 template <int BN, bool DEEP = false>
 struct Cfg {
-  static constexpr int kStages = BN == 256 ? (DEEP ? 4 : 3) : (DEEP ? 6 : 5);
+  static constexpr int kStages = BN == 256 ? (DEEP ? 4 : 3) : BN == 192 ? 4 : (DEEP ? 6 : 5);
   static constexpr int kABytes = kBM * kBK;
   static constexpr int kBBytes = BN * kBK;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kTmemCols = 2 * BN;
+  // two accumulators of BN columns; the allocation is a power of two
+  static constexpr int kTmemCols = BN == 192 ? 512 : 2 * BN;
   static constexpr int kOutOffset = kStages * kStageBytes;
   // per-tile column operands (colsum, a_scale*w_scale, bias), double-buffered
   static constexpr int kParamOffset = kOutOffset + kEpiWarps * kStageOutBytes;
@@ -116,6 +117,7 @@ struct Cfg {
   static constexpr int kSmemBytes = kBarOffset + 512 + 1024 /*align slack*/;
   // barriers, TMEM slot, (min, max) reduction slots, residual-load barriers
   static_assert((2 * kStages + 4) * 8 + 8 + kEpiWarps * 8 <= 256, "barrier area");
+  static_assert(kSmemBytes <= 227 * 1024, "shared memory");
 };
 
 // Named barrier among the epilogue warps only.
@@ -800,7 +802,7 @@ static int launch_tc(cudaStream_t s, const void* a, bool a_signed, const void* b
 
 // Which kernel runs a GEMM and with how many CTAs.
 struct GemmPlan {
-  int bn;     // 128 / 256 for the tensor-core kernel, 0 for the SIMT kernel
+  int bn;     // 128 / 192 / 256 for the tensor-core kernel, 0 for the SIMT kernel
   int grid;   // CTAs (tensor-core path)
 };
 
@@ -809,11 +811,25 @@ static GemmPlan plan_gemm(const GemmArgs& args, const void* a, const void* bt) {
   const bool tma_ok = (args.K % 16 == 0) && args.K > 0 &&
                       ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(bt)) & 15) == 0;
   if (!tma_ok) return p;
-  // narrow tiles when the wide ones would leave most SMs idle
-  const long tiles256 = (long)((args.M + kBM - 1) / kBM) * ((args.N + 255) / 256);
-  p.bn = (args.N <= 128 || tiles256 < sm_count()) ? 128 : 256;
-  const long tiles = (long)((args.M + kBM - 1) / kBM) * ((args.N + p.bn - 1) / p.bn);
-  p.grid = (int)(tiles < sm_count() ? tiles : sm_count());
+  // Tile width: the persistent kernel's time is set by its busiest CTA,
+  // ceil(tiles / SMs) tiles, each costing about BN + 64 (its columns plus the
+  // per-tile A fetch and epilogue overhead, in the same units); take the BN
+  // that minimises that (ties: the wider tile).  E.g. N = 768 at M = 4096
+  // runs 128 tiles of 192 columns (one per CTA) instead of 192 tiles of 128.
+  const long sms = sm_count();
+  const long mt = (args.M + kBM - 1) / kBM;
+  long best = -1;
+  for (int bn : {256, 192, 128}) {
+    const long tiles = mt * ((args.N + bn - 1) / bn);
+    const long cost = ((tiles + sms - 1) / sms) * (bn + 64);
+    if (best < 0 || cost < best) {
+      best = cost;
+      p.bn = bn;
+    }
+  }
+  if (args.N <= 128) p.bn = 128;
+  const long tiles = mt * ((args.N + p.bn - 1) / p.bn);
+  p.grid = (int)(tiles < sms ? tiles : sms);
   return p;
 }
 
@@ -833,6 +849,9 @@ static int launch_gemm(cudaStream_t s, const void* a, bool a_signed,
   if (p.bn == 256)
     return deep ? launch_tc<256, EPI, true>(s, a, a_signed, bt, b_signed, args)
                 : launch_tc<256, EPI, false>(s, a, a_signed, bt, b_signed, args);
+  if (p.bn == 192)
+    return deep ? launch_tc<192, EPI, true>(s, a, a_signed, bt, b_signed, args)
+                : launch_tc<192, EPI, false>(s, a, a_signed, bt, b_signed, args);
   if (p.bn == 128)
     return deep ? launch_tc<128, EPI, true>(s, a, a_signed, bt, b_signed, args)
                 : launch_tc<128, EPI, false>(s, a, a_signed, bt, b_signed, args);
