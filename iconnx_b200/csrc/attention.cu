@@ -252,6 +252,7 @@ struct AttTc {
   static constexpr int kOC = 64 / kWPQ;        // context columns per thread
   static constexpr int kQLoads = 2048 / kThreads;       // float4 of Q per thread
   static constexpr int kKLoads = KT * 16 / kThreads;    // float4 of K per thread per tile
+  static constexpr int kVKeys = KT * 64 / kThreads;     // keys of V per thread per tile (one d)
   static constexpr int kKAtom = KT * 128;      // K slices: KT rows x 128 B per block
   static constexpr int kVAtom = 64 * 128;      // V^T: 64 rows (d) x 32 keys (128 B) per block
   static constexpr int kVBlocks = KT / 32;
@@ -269,10 +270,15 @@ struct AttTc {
   static constexpr int kTmemPh = 0;              // P hi (after the scores are consumed)
   static constexpr int kTmemPl = KT;             // P lo
   static constexpr int kTmemO = 2 * KT;          // O_tile (64 columns)
-  static constexpr int kMinBlocks = NW == 8 ? 2 : 3;
+  static constexpr int kMinBlocks = KT == 64 ? 2 : 3;
   static_assert(kTmemO + 64 <= (int)kTmemCols, "TMEM layout");
   static_assert(kMinBlocks * kSmem <= 227 * 1024, "CTAs per SM");
   static_assert(kSC % 16 == 0 && kOC % 16 == 0, "16-column TMEM accesses");
+  // every staging map covers exactly the tile: K rows (16 threads per row),
+  // V^T (64 threads per key group), the mask (one thread per key)
+  static_assert(kKLoads * kThreads == KT * 16 && kKLoads >= 1, "K staging covers the tile");
+  static_assert(kVKeys * kThreads == KT * 64 && kVKeys % 4 == 0, "V staging covers the tile");
+  static_assert(kThreads >= KT && kThreads % 64 == 0, "mask / V thread maps");
 };
 
 // The value of x, hidden from the optimiser (no hoisting of what depends on it).
@@ -342,7 +348,7 @@ __device__ __forceinline__ float slice_row_store(uint8_t* base, int block, int r
 }
 
 template <int KT, int NW, bool C_POW2>
-__global__ void __launch_bounds__(32 * NW, (NW == 8 ? 2 : 3))
+__global__ void __launch_bounds__(32 * NW, (KT == 64 ? 2 : 3))
     attention_tc_kernel(const float* __restrict__ q, const float* __restrict__ k,
                         const float* __restrict__ v, int ld, float* __restrict__ out, int H, int S,
                         int nh, float c, const float* __restrict__ mask, int mask_per_batch,
@@ -371,10 +377,10 @@ __global__ void __launch_bounds__(32 * NW, (NW == 8 ? 2 : 3))
   const float* mrow = mask ? mask + (mask_per_batch ? (size_t)b * S : 0) : nullptr;
   const float inv_c = 1.0f / c;  // exact when c is a power of two (C_POW2)
   // Q / K rows: 16 threads per 256-byte row; V: thread = column d (tid % 64)
-  // of keys 16 (tid / 64) .. +15, stored as row d of V^T
+  // of kVKeys consecutive keys (key group tid / 64), stored as row d of V^T
   const int kv_row = tid >> 4, kv_col = (tid & 15) * 4;
   constexpr int kRowStep = A::kThreads / 16;  // rows between a thread's Q / K loads
-  const int v_d = tid & 63, v_key = (tid >> 6) * 16;
+  const int v_d = tid & 63, v_key = (tid >> 6) * A::kVKeys;
 
   if (tid == 0) {
     mbar_init(bar_s, 1);
@@ -471,9 +477,9 @@ __global__ void __launch_bounds__(32 * NW, (NW == 8 ? 2 : 3))
       mma_commit(bar_s);
     }
     {
-      float4 nv[4];
+      float4 nv[A::kVKeys / 4];
 #pragma unroll
-      for (int g = 0; g < 4; ++g) {
+      for (int g = 0; g < A::kVKeys / 4; ++g) {
         float x[4];
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
@@ -483,7 +489,7 @@ __global__ void __launch_bounds__(32 * NW, (NW == 8 ? 2 : 3))
         nv[g] = make_float4(x[0], x[1], x[2], x[3]);
       }
 #pragma unroll
-      for (int g = 0; g < 4; ++g)
+      for (int g = 0; g < A::kVKeys / 4; ++g)
         split_store(sm + A::kOffVh, sm + A::kOffVl, A::kVAtom, v_d, v_key + 4 * g, nv[g]);
     }
     ok = mbar_wait_warp(bar_s, phase, ICX_DEVICE_TIMEOUT_EPILOGUE);
