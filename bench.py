@@ -519,6 +519,10 @@ def main():
     ap.add_argument("--workload", default="distilbert", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--global-dql", action="store_true",
+                    help="encoders on N>1 GPUs: every DynamicQuantizeLinear takes (min, max) over "
+                         "all ranks (8-byte NCCL all-reduce), matching one executor over the "
+                         "whole batch")
     ap.add_argument("--scaling", default="weak", choices=["weak", "strong"],
                     help="weak: every GPU runs the config's batch; strong (encoders): the "
                          "config's batch is split across the GPUs")
@@ -553,6 +557,15 @@ def main():
         wl = WORKLOADS[args.workload](dev, seed_base=1000 * rank, batch=full // world)
     else:
         wl = WORKLOADS[args.workload](dev, seed_base=1000 * rank)
+    global_dql = args.global_dql and world > 1 and isinstance(wl, EncoderWorkload)
+    if global_dql:
+        from iconnx_b200.engine import nccl_unique_id
+        box = [nccl_unique_id() if rank == 0 else None]
+        pg.broadcast_object_list(box, src=0)
+        wl.ex.set_global_dql(box[0], world, rank)
+        wl.ex.run(wl.inputs, [wl.out])     # recompile with the all-reduce steps
+        wl.ex.run(wl.inputs, [wl.out])     # capture the CUDA graph
+        wl.launches_per_step = wl.ex.kernel_launches()
     stream = torch.cuda.current_stream(dev)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     if not hasattr(wl, "launches_per_step"):
@@ -676,6 +689,9 @@ def main():
                                "seq_len": wl.seq, "batch_per_gpu": wl.batch})
         if strong:
             line["config"]["parallelism"] += f"; strong scaling of the config's batch {wl.global_batch}"
+        if global_dql:
+            line["config"]["parallelism"] = (f"batch-shard x{world}, global DynamicQuantizeLinear "
+                                             "(8-byte NCCL MAX all-reduce per DQL)")
         line["int8_gemm_tops_in_step"] = wl.gemm_ops / (total_ms / args.steps / 1e3) / 1e12
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         from oracle import oracle

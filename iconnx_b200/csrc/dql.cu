@@ -279,6 +279,56 @@ __global__ void __launch_bounds__(kQuantThreads, 3)
   }
 }
 
+// Global DynamicQuantizeLinear over batch-sharded executors: the local
+// partials fold into one pair (-min, max) so that a single MAX all-reduce
+// across the executors yields the global (min, max) of the whole batch;
+// unfold writes it back as one (min, max) partial for the quantise pass.
+__global__ void minmax_fold_kernel(const float2* __restrict__ parts, int n, float* __restrict__ g) {
+  pdl_wait();
+  pdl_trigger();
+  __shared__ float s_mn[8], s_mx[8];
+  float mn = 0.0f, mx = 0.0f;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float2 v = parts[i];
+    mn = fminf(mn, v.x);
+    mx = fmaxf(mx, v.y);
+  }
+  warp_minmax(mn, mx);
+  const int w = threadIdx.x >> 5;
+  if ((threadIdx.x & 31) == 0) {
+    s_mn[w] = mn;
+    s_mx[w] = mx;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int i = 1; i < (int)(blockDim.x >> 5); ++i) {
+      mn = fminf(mn, s_mn[i]);
+      mx = fmaxf(mx, s_mx[i]);
+    }
+    g[0] = -mn;
+    g[1] = mx;
+  }
+}
+
+__global__ void minmax_unfold_kernel(const float* __restrict__ g, float2* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
+  if (threadIdx.x == 0) out[0] = make_float2(-g[0], g[1]);
+}
+
+int launch_minmax_fold(cudaStream_t s, const float* partials, int n, float* g) {
+  launch_pdl(minmax_fold_kernel, dim3(1), dim3(256), 0, s, reinterpret_cast<const float2*>(partials),
+             n, g);
+  ICX_LAUNCH_CHECK();
+  return ICX_OK;
+}
+
+int launch_minmax_unfold(cudaStream_t s, const float* g, float* out) {
+  launch_pdl(minmax_unfold_kernel, dim3(1), dim3(32), 0, s, g, reinterpret_cast<float2*>(out));
+  ICX_LAUNCH_CHECK();
+  return ICX_OK;
+}
+
 static int minmax_blocks(size_t n) {
   size_t per_block = (size_t)kMinmaxThreads * 16;
   size_t b = (n + per_block - 1) / per_block;

@@ -26,6 +26,8 @@
 // !Sync); use one per thread / GPU.
 #include <cublas_v2.h>
 #include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <nccl.h>
 
 #include <algorithm>
 #include <cmath>
@@ -33,6 +35,7 @@
 #include <functional>
 #include <map>
 #include <memory>
+#include <mutex>
 #include <set>
 #include <string>
 #include <unordered_map>
@@ -161,6 +164,36 @@ struct Step {
   std::string node, op, out;
   std::function<int(cudaStream_t)> fn;
 };
+
+// NCCL, loaded on first use (the library has no link-time dependency on it):
+// only the global DynamicQuantizeLinear mode of batch-sharded executors uses
+// it, for one 8-byte MAX all-reduce per DynamicQuantizeLinear.
+struct NcclApi {
+  ncclResult_t (*get_unique_id)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*all_reduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                             cudaStream_t) = nullptr;
+  ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+  const char* (*error_string)(ncclResult_t) = nullptr;
+};
+
+static const NcclApi* nccl_api() {
+  static NcclApi api;
+  static bool ok = false;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) return;
+    api.get_unique_id = reinterpret_cast<decltype(api.get_unique_id)>(dlsym(h, "ncclGetUniqueId"));
+    api.comm_init_rank = reinterpret_cast<decltype(api.comm_init_rank)>(dlsym(h, "ncclCommInitRank"));
+    api.all_reduce = reinterpret_cast<decltype(api.all_reduce)>(dlsym(h, "ncclAllReduce"));
+    api.comm_destroy = reinterpret_cast<decltype(api.comm_destroy)>(dlsym(h, "ncclCommDestroy"));
+    api.error_string = reinterpret_cast<decltype(api.error_string)>(dlsym(h, "ncclGetErrorString"));
+    ok = api.get_unique_id && api.comm_init_rank && api.all_reduce && api.comm_destroy &&
+         api.error_string;
+  });
+  return ok ? &api : nullptr;
+}
 
 class Engine {
  public:
@@ -492,6 +525,8 @@ class Engine {
       if (p.done) cudaEventDestroy(p.done);
     }
     if (copy_stream_) cudaStreamDestroy(copy_stream_);
+    if (comm_) nccl_api()->comm_destroy(comm_);
+    if (gdql_) cudaFree(gdql_);
     if (stream_) cudaStreamDestroy(stream_);
   }
 
@@ -1596,7 +1631,36 @@ class Engine {
           rows = const_cast<int32_t*>(rowsum_for(n.out[0], (int64_t)(cnt / (row_len ? row_len : 1))));
         }
       auto mit = dql_mode_.find(idx);
-      if (mit != dql_mode_.end()) {
+      if (comm_) {
+        // global: local partials -> (-min, max) -> MAX all-reduce over the
+        // executors -> one (min, max) partial -> the quantise pass
+        const bool producer = mit != dql_mode_.end();
+        float* mm = producer ? slot_ptr(mit->second) : dql_workspace();
+        const int* mmc = producer ? &minmax_count_[mit->second] : nullptr;
+        float* g = gdql_;
+        ncclComm_t comm = comm_;
+        const NcclApi* api = nccl_api();
+        add_step(n, "DynamicQuantizeLinear(global)", o0, [=](cudaStream_t s) {
+          int nparts;
+          if (producer) {
+            nparts = *mmc;
+          } else {
+            const int rc = launch_dql_minmax(s, x, cnt, reinterpret_cast<float2*>(mm));
+            if (rc) return rc;
+            nparts = dql_minmax_partials(cnt);
+          }
+          int rc = launch_minmax_fold(s, mm, nparts, g);
+          if (rc) return rc;
+          const ncclResult_t r = api->all_reduce(g, g, 2, ncclFloat32, ncclMax, comm, s);
+          if (r != ncclSuccess) {
+            set_error("ncclAllReduce failed: %s", api->error_string(r));
+            return ICX_ERR_CUDA;
+          }
+          rc = launch_minmax_unfold(s, g, g + 2);
+          if (rc) return rc;
+          return icx_dql_quantize_f32_u8(s, x, cnt, g + 2, 1, y, sc, zp, rows, row_len);
+        }, (producer ? 3 : 4) + (rows ? 1 : 0));
+      } else if (mit != dql_mode_.end()) {
         const float* mm = slot_ptr(mit->second);
         const int* mmc = &minmax_count_[mit->second];
         add_step(n, "DynamicQuantizeLinear(quantise)", o0, [=](cudaStream_t s) {
@@ -1819,6 +1883,8 @@ class Engine {
   Pending pend_[2];
   cudaStream_t copy_stream_ = nullptr;
   int64_t next_ticket_ = 0;
+  ncclComm_t comm_ = nullptr;  // global DQL (set_global_dql)
+  float* gdql_ = nullptr;      // (-min, max) pair [0..1] and the (min, max) partial [2..3]
   std::map<int, int> dql_mode_;
   int n_slots_ = 0;
   std::vector<int> minmax_count_;
@@ -1836,6 +1902,42 @@ class Engine {
 
  public:
   void set_pending_outputs(const std::vector<std::string>& o) { pending_outputs_ = o; }
+
+  // Global DynamicQuantizeLinear: every DQL takes its (min, max) over all
+  // `nranks` executors sharing `id` (one per GPU, each with its shard of the
+  // batch), so the shards quantise exactly as one executor over the whole
+  // batch would.  Every rank must call this concurrently (communicator
+  // set-up is collective) and then run the same graph.  nranks <= 1: off.
+  int set_global_dql(const void* id, int nranks, int rank) {
+    ICX_CUDA(cudaSetDevice(device_));
+    if (comm_) {
+      ICX_CUDA(cudaStreamSynchronize(stream_));
+      nccl_api()->comm_destroy(comm_);
+      comm_ = nullptr;
+    }
+    invalidate();
+    if (nranks <= 1) return ICX_OK;
+    ICX_REQUIRE(id != nullptr && rank >= 0 && rank < nranks, "set_global_dql: bad rank %d of %d",
+                rank, nranks);
+    const NcclApi* api = nccl_api();
+    if (!api) {
+      set_error("set_global_dql: libnccl.so.2 could not be loaded");
+      return ICX_ERR_UNSUPPORTED;
+    }
+    ncclUniqueId uid;
+    memcpy(&uid, id, sizeof(uid));
+    ncclComm_t c = nullptr;
+    const ncclResult_t r = api->comm_init_rank(&c, nranks, uid, rank);
+    if (r != ncclSuccess) {
+      set_error("ncclCommInitRank failed: %s", api->error_string(r));
+      return ICX_ERR_CUDA;
+    }
+    comm_ = c;
+    if (!gdql_) ICX_CUDA(cudaMalloc(&gdql_, 64));
+    return ICX_OK;
+  }
+
+
 };
 
 }  // namespace icx
@@ -1945,6 +2047,29 @@ extern "C" int icx_engine_submit(icx_engine* h, int n_in, const char* const* nam
   }
   h->e->set_pending_outputs(outs);
   return h->e->submit(nm, dt, sh, hp, outs, ho, hb, ticket);
+}
+
+extern "C" int icx_nccl_unique_id(void* id_out, size_t bytes) {
+  ICX_REQUIRE(id_out && bytes >= sizeof(ncclUniqueId), "nccl_unique_id: need %zu bytes",
+              sizeof(ncclUniqueId));
+  const icx::NcclApi* api = icx::nccl_api();
+  if (!api) {
+    icx::set_error("nccl_unique_id: libnccl.so.2 could not be loaded");
+    return ICX_ERR_UNSUPPORTED;
+  }
+  ncclUniqueId id;
+  const ncclResult_t r = api->get_unique_id(&id);
+  if (r != ncclSuccess) {
+    icx::set_error("ncclGetUniqueId failed: %s", api->error_string(r));
+    return ICX_ERR_CUDA;
+  }
+  memcpy(id_out, &id, sizeof(id));
+  return ICX_OK;
+}
+
+extern "C" int icx_engine_set_global_dql(icx_engine* h, const void* nccl_id, int nranks, int rank) {
+  ICX_REQUIRE(h, "set_global_dql: null engine");
+  return h->e->set_global_dql(nccl_id, nranks, rank);
 }
 
 extern "C" int icx_engine_wait(icx_engine* h, int64_t ticket) {

@@ -45,5 +45,8 @@ int launch_attention_f32(cudaStream_t s, const float* q, const float* k, const f
 // dql.cu
 int dql_minmax_partials(size_t n);
 int launch_dql_minmax(cudaStream_t s, const float* x, size_t n, float2* partials);
+// global DQL: n (min, max) partials -> g = (-min, max); g -> one (min, max) partial
+int launch_minmax_fold(cudaStream_t s, const float* partials, int n, float* g);
+int launch_minmax_unfold(cudaStream_t s, const float* g, float* out);
 
 }  // namespace icx

@@ -181,6 +181,15 @@ class GpuGraphExecutor:
         check(self._L.icx_engine_wait(self._h, int(ticket)))
         getattr(self, "_in_flight", {}).pop(int(ticket), None)
 
+    def set_global_dql(self, nccl_id: bytes | None, nranks: int, rank: int) -> None:
+        """Global DynamicQuantizeLinear across batch-sharded executors: every
+        DQL takes (min, max) over all ``nranks`` executors through an 8-byte
+        NCCL all-reduce, so the shards quantise exactly as one executor over
+        the whole batch.  All ranks call this concurrently with the id from
+        :func:`nccl_unique_id`; ``nranks <= 1`` turns it off."""
+        buf = ctypes.create_string_buffer(bytes(nccl_id or b""), 128) if nccl_id else None
+        check(self._L.icx_engine_set_global_dql(self._h, buf, int(nranks), int(rank)))
+
     def fetch(self, name: str, out: np.ndarray | None = None) -> np.ndarray:
         dt, rk = ctypes.c_int(), ctypes.c_int()
         dims = (ctypes.c_int64 * 6)()
@@ -237,3 +246,11 @@ class GpuGraphExecutor:
 
     def set_cuda_graphs(self, enabled: bool) -> None:
         check(self._L.icx_engine_set_cuda_graphs(self._h, int(enabled)))
+
+
+def nccl_unique_id() -> bytes:
+    """A new NCCL unique id (128 bytes) for :meth:`GpuGraphExecutor.set_global_dql`."""
+    from . import _lib as L
+    buf = ctypes.create_string_buffer(128)
+    check(L.load().icx_nccl_unique_id(buf, 128))
+    return buf.raw

@@ -9,7 +9,10 @@ collective is on the data path.
 
 Per-shard dynamic quantisation takes its min/max over the shard, so a sharded
 run equals, shard by shard, an independent executor on that sub-batch; it is
-not bit-equal to a single executor over the whole batch.
+not bit-equal to a single executor over the whole batch.  With
+``global_dql=True`` every DynamicQuantizeLinear takes (min, max) over all
+shards through one 8-byte NCCL all-reduce (NVLink), and the sharded run is
+bit-equal to one executor over the whole batch.
 
 A failing shard raises in the caller; a shard that does not finish within
 ``timeout`` seconds raises TimeoutError without waiting for it.
@@ -44,7 +47,7 @@ class ShardedRunner:
     """
 
     def __init__(self, build: Callable, devices: list, batch: int,
-                 factory: Callable | None = None):
+                 factory: Callable | None = None, global_dql: bool = False):
         if factory is None:
             from .engine import GpuGraphExecutor
             factory = GpuGraphExecutor.new
@@ -52,12 +55,21 @@ class ShardedRunner:
         self.bounds = [b for b in shard_bounds(batch, len(self.devices))]
         self._build, self._factory = build, factory
         self._ex = [None] * len(self.devices)
+        self._nccl_id = None
+        if global_dql and len(self.devices) > 1:
+            if any(e <= s for s, e in self.bounds):
+                raise ValueError("global_dql needs at least one row per shard")
+            from .engine import nccl_unique_id
+            self._nccl_id = nccl_unique_id()
 
     def _ensure(self, i):
         if self._ex[i] is None:
             ex = self._factory(self.devices[i])
             s, e = self.bounds[i]
             self._build(ex, e - s)
+            if self._nccl_id is not None:
+                # collective set-up: every worker thread reaches this together
+                ex.set_global_dql(self._nccl_id, len(self.devices), i)
             self._ex[i] = ex
         return self._ex[i]
 

@@ -269,6 +269,19 @@ ICX_API int icx_engine_submit(icx_engine* e, int n_in, const char* const* names,
                               const size_t* host_out_bytes, int64_t* ticket);
 /* Blocks until submission `ticket` has its outputs in its host buffers. */
 ICX_API int icx_engine_wait(icx_engine* e, int64_t ticket);
+
+/* Global DynamicQuantizeLinear for batch-sharded executors (no reference
+ * counterpart: the reference runs on one GPU).  By default each executor
+ * quantises its shard with the shard's own (min, max); with this mode every
+ * DynamicQuantizeLinear takes (min, max) over all executors through one
+ * 8-byte NCCL MAX all-reduce on the executor's stream, so the shards give
+ * bit-for-bit what one executor over the whole batch gives.
+ * icx_nccl_unique_id writes a 128-byte id (bytes >= 128) on one rank; every
+ * rank then calls icx_engine_set_global_dql with it concurrently (the set-up
+ * is collective).  nranks <= 1 turns the mode off.  NCCL (libnccl.so.2) is
+ * loaded on first use. */
+ICX_API int icx_nccl_unique_id(void* id_out, size_t bytes);
+ICX_API int icx_engine_set_global_dql(icx_engine* e, const void* nccl_id, int nranks, int rank);
 /* The compiled plan, one "op node -> output" line per launch step. */
 ICX_API const char* icx_engine_plan(icx_engine* e);
 /* Replay the compiled plan as a CUDA graph after the first run (default on). */

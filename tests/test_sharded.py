@@ -116,3 +116,32 @@ def test_sharded_on_gpus_matches_per_shard_executors():
         build(ex, e - s)
         ref = ex.run({k: v[s:e] for k, v in inp.items()}, ["last_hidden_state"])["last_hidden_state"]
         np.testing.assert_array_equal(out[s:e], ref)
+
+
+@pytest.mark.gpu
+def test_global_dql_sharded_equals_full_batch():
+    """global_dql: each DynamicQuantizeLinear takes (min, max) over all shards
+    through an NCCL all-reduce, so the sharded encoder is bit-equal to one
+    executor over the whole batch (every other op is per row)."""
+    import torch
+    from iconnx_b200 import graphs
+    from iconnx_b200.engine import GpuGraphExecutor
+    n = torch.cuda.device_count()
+    if n < 2:
+        pytest.skip("needs 2 GPUs")
+    cfg = graphs.BertConfig(layers=2, vocab=1000)
+    build = lambda b, batch: graphs.build_bert(b, cfg, batch, 32)  # noqa: E731
+    runner = ShardedRunner(build, list(range(n)), batch=2 * n, global_dql=True)
+    inp = graphs.bert_inputs(2 * n, 32, vocab=1000)
+    outs = [runner.run(inp, ["last_hidden_state"], timeout=300)["last_hidden_state"] for _ in range(3)]
+    ex = GpuGraphExecutor.new(0)
+    build(ex, 2 * n)
+    ref = ex.run(inp, ["last_hidden_state"])["last_hidden_state"]
+    for out in outs:   # eager, capture and replayed graph runs
+        np.testing.assert_array_equal(out.view(np.uint32), ref.view(np.uint32))
+
+
+def test_global_dql_needs_rows_on_every_shard():
+    with pytest.raises(ValueError):
+        ShardedRunner(lambda b, n: None, [0, 1, 2], batch=2, factory=lambda d: None,
+                      global_dql=True)
