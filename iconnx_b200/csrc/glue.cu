@@ -289,6 +289,64 @@ int launch_binary(cudaStream_t s, int op, const float* a, const std::vector<int6
 constexpr int kLnVec = 8;
 constexpr int kLnWarps = 8;
 
+// One row of LayerNormalization by one warp (D % 4 == 0, D <= 32*4*kLnVec)
+// on values already in registers (lane l holds float4 columns l + 32 j):
+// mean, then the mean of squared deviations, y = (x - mean) * rstd * g + b,
+// each step rounded in f32 as the reference's CPU operator.  Tracks the
+// (min, max) of y.
+__device__ __forceinline__ void ln_row(const float4 (&v)[kLnVec], const float4* __restrict__ g4,
+                                       const float4* __restrict__ b4, float* __restrict__ y, int D,
+                                       float eps, int lane, float& mn, float& mx) {
+  const int nv = D / 4;
+  float sum = 0.0f;
+#pragma unroll
+  for (int j = 0; j < kLnVec; ++j) sum += (v[j].x + v[j].y) + (v[j].z + v[j].w);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  const float mean = sum / (float)D;
+  float sq = 0.0f;
+#pragma unroll
+  for (int j = 0; j < kLnVec; ++j) {
+    const int c = lane + 32 * j;
+    if (c < nv) {
+      const float a = v[j].x - mean, b = v[j].y - mean, cc = v[j].z - mean, d = v[j].w - mean;
+      sq += (a * a + b * b) + (cc * cc + d * d);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+  const float rstd = rsqrtf(sq / (float)D + eps);
+  float4* yr = reinterpret_cast<float4*>(y);
+#pragma unroll
+  for (int j = 0; j < kLnVec; ++j) {
+    const int c = lane + 32 * j;
+    if (c < nv) {
+      const float4 g = __ldg(g4 + c);
+      const float4 bb = b4 ? __ldg(b4 + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+      float4 o;
+      o.x = (v[j].x - mean) * rstd * g.x + bb.x;
+      o.y = (v[j].y - mean) * rstd * g.y + bb.y;
+      o.z = (v[j].z - mean) * rstd * g.z + bb.z;
+      o.w = (v[j].w - mean) * rstd * g.w + bb.w;
+      yr[c] = o;
+      mn = fminf(mn, fminf(fminf(o.x, o.y), fminf(o.z, o.w)));
+      mx = fmaxf(mx, fmaxf(fmaxf(o.x, o.y), fmaxf(o.z, o.w)));
+    }
+  }
+}
+
+__device__ __forceinline__ void ln_load(const float* __restrict__ x, int nv, int lane,
+                                        float4 (&v)[kLnVec]) {
+  const float4* xr = reinterpret_cast<const float4*>(x);
+#pragma unroll
+  for (int j = 0; j < kLnVec; ++j) {
+    const int c = lane + 32 * j;
+    v[j] = c < nv ? xr[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+}
+
+// Warps stride over rows; the next row's loads are issued before the current
+// row is normalised, so a warp's second row does not wait for its own load.
 __global__ void __launch_bounds__(32 * kLnWarps)
     layernorm_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
                      const float* __restrict__ beta, float* __restrict__ y, int rows, int D,
@@ -300,48 +358,18 @@ __global__ void __launch_bounds__(32 * kLnWarps)
   const int nv = D / 4;
   const float4* g4 = reinterpret_cast<const float4*>(gamma);
   const float4* b4 = reinterpret_cast<const float4*>(beta);
-  for (int row = blockIdx.x * kLnWarps + w; row < rows; row += gridDim.x * kLnWarps) {
-    const float4* xr = reinterpret_cast<const float4*>(x + (size_t)row * D);
-    float4 v[kLnVec];
-    float sum = 0.0f;
+  const int stride = gridDim.x * kLnWarps;
+  int row = blockIdx.x * kLnWarps + w;
+  float4 cur[kLnVec];
+  if (row < rows) ln_load(x + (size_t)row * D, nv, lane, cur);
+  while (row < rows) {
+    const int next = row + stride;
+    float4 nxt[kLnVec];
+    if (next < rows) ln_load(x + (size_t)next * D, nv, lane, nxt);
+    ln_row(cur, g4, b4, y + (size_t)row * D, D, eps, lane, mn, mx);
 #pragma unroll
-    for (int j = 0; j < kLnVec; ++j) {
-      const int c = lane + 32 * j;
-      v[j] = c < nv ? xr[c] : make_float4(0.f, 0.f, 0.f, 0.f);
-      sum += (v[j].x + v[j].y) + (v[j].z + v[j].w);
-    }
-#pragma unroll
-    for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-    const float mean = sum / (float)D;
-    float sq = 0.0f;
-#pragma unroll
-    for (int j = 0; j < kLnVec; ++j) {
-      const int c = lane + 32 * j;
-      if (c < nv) {
-        const float a = v[j].x - mean, b = v[j].y - mean, cc = v[j].z - mean, d = v[j].w - mean;
-        sq += (a * a + b * b) + (cc * cc + d * d);
-      }
-    }
-#pragma unroll
-    for (int o = 16; o; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
-    const float rstd = rsqrtf(sq / (float)D + eps);
-    float4* yr = reinterpret_cast<float4*>(y + (size_t)row * D);
-#pragma unroll
-    for (int j = 0; j < kLnVec; ++j) {
-      const int c = lane + 32 * j;
-      if (c < nv) {
-        const float4 g = __ldg(g4 + c);
-        const float4 bb = beta ? __ldg(b4 + c) : make_float4(0.f, 0.f, 0.f, 0.f);
-        float4 o;
-        o.x = (v[j].x - mean) * rstd * g.x + bb.x;
-        o.y = (v[j].y - mean) * rstd * g.y + bb.y;
-        o.z = (v[j].z - mean) * rstd * g.z + bb.z;
-        o.w = (v[j].w - mean) * rstd * g.w + bb.w;
-        yr[c] = o;
-        mn = fminf(mn, fminf(fminf(o.x, o.y), fminf(o.z, o.w)));
-        mx = fmaxf(mx, fmaxf(fmaxf(o.x, o.y), fmaxf(o.z, o.w)));
-      }
-    }
+    for (int j = 0; j < kLnVec; ++j) cur[j] = nxt[j];
+    row = next;
   }
   if (minmax) {
     __shared__ float2 red[kLnWarps];
