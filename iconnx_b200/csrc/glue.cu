@@ -53,7 +53,7 @@ __global__ void gather_rows_kernel(const T* __restrict__ table, int64_t rows,
     if (r < 0) r += rows;
     if (r < 0 || r >= rows) {
       if (d == 0 && err) atomicExch(err, 1);
-      out[t] = T(0);
+      out[t] = T{};
       continue;
     }
     out[t] = table[(size_t)r * D + d];
@@ -63,6 +63,15 @@ __global__ void gather_rows_kernel(const T* __restrict__ table, int64_t rows,
 int launch_gather_rows(cudaStream_t s, const void* table, int elem_bytes, int64_t rows,
                        const int64_t* idx, size_t n, size_t D, void* out, int* err) {
   if (n * D == 0) return ICX_OK;
+  // rows that are whole 16-byte vectors move as such (f32 embeddings)
+  if ((D * elem_bytes) % 16 == 0 &&
+      ((reinterpret_cast<uintptr_t>(table) | reinterpret_cast<uintptr_t>(out)) & 15) == 0) {
+    const size_t D16 = D * elem_bytes / 16;
+    launch_pdl(gather_rows_kernel<uint4>, dim3(elt_blocks(n * D16)), dim3(kEltThreads), 0, s,
+               static_cast<const uint4*>(table), rows, idx, n, D16, static_cast<uint4*>(out), err);
+    ICX_LAUNCH_CHECK();
+    return ICX_OK;
+  }
   const dim3 g(elt_blocks(n * D)), b(kEltThreads);
   switch (elem_bytes) {
     case 1:
@@ -113,7 +122,8 @@ __global__ void binary_same_kernel(const float4* __restrict__ a, const float4* _
   }
 }
 
-// [rows, D] (op) [D] : the bias / per-column broadcast of a matrix.
+// [rows, P] (op) [P]: an operand that repeats every P elements of the output
+// (a bias row, position embeddings over the batch); P % 4 == 0.
 template <int OP>
 __global__ void binary_rowvec_kernel(const float4* __restrict__ a, const float4* __restrict__ b,
                                      float4* __restrict__ o, size_t n4, size_t d4, int swap) {
@@ -194,10 +204,18 @@ int launch_binary(cudaStream_t s, int op, const float* a, const std::vector<int6
   if (n == 0) return ICX_OK;
   const bool aligned = ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) |
                          reinterpret_cast<uintptr_t>(out)) & 15) == 0;
-  const int64_t D = oshape.empty() ? 1 : oshape.back();
   const bool a_full = ashape == oshape, b_full = bshape == oshape;
+  // the operand repeats along the leading axes: its shape (leading 1s
+  // dropped) equals the output's trailing dimensions, e.g. a bias [D] or
+  // position embeddings [S, H] added to [B, S, H]
   auto is_rowvec = [&](const std::vector<int64_t>& sh) {
-    return numel(sh) == D && !sh.empty() && sh.back() == D;
+    size_t k = 0;
+    while (k < sh.size() && sh[k] == 1) ++k;
+    const size_t r = sh.size() - k;
+    if (r == 0 || r > oshape.size()) return false;
+    for (size_t d = 0; d < r; ++d)
+      if (sh[k + d] != oshape[oshape.size() - r + d]) return false;
+    return numel(sh) % 4 == 0;
   };
   if (aligned && n % 4 == 0) {
     if (a_full && b_full) {
@@ -215,14 +233,15 @@ int launch_binary(cudaStream_t s, int op, const float* a, const std::vector<int6
       ICX_LAUNCH_CHECK();
       return ICX_OK;
     }
-    if (D % 4 == 0 && ((a_full && is_rowvec(bshape)) || (b_full && is_rowvec(ashape)))) {
+    if ((a_full && is_rowvec(bshape)) || (b_full && is_rowvec(ashape))) {
       const int swap = a_full ? 0 : 1;
       const float* m = a_full ? a : b;
       const float* v = a_full ? b : a;
+      const size_t period = (size_t)numel(a_full ? bshape : ashape);
 #define ICX_ROW(OPC)                                                                       \
   launch_pdl(binary_rowvec_kernel<OPC>, dim3(elt_blocks(n / 4)), dim3(kEltThreads), 0, s,                      \
       reinterpret_cast<const float4*>(m), reinterpret_cast<const float4*>(v),              \
-      reinterpret_cast<float4*>(out), n / 4, (size_t)D / 4, swap)
+      reinterpret_cast<float4*>(out), n / 4, period / 4, swap)
       switch (op) {
         case kAdd: ICX_ROW(kAdd); break;
         case kSub: ICX_ROW(kSub); break;
