@@ -683,10 +683,15 @@ int launch_attention_f32(cudaStream_t s, const float* q, const float* k, const f
                 "Attention: %d (min, max) partials exceed %d", parts, ICX_MAX_MINMAX_PARTIALS);
     int cexp;
     const bool c_pow2 = frexpf(c, &cexp) == 0.5f;
-    static const bool wide = [] {  // the <64, 8> tiling instead of <32, 4>
+    // <32, 4> (three CTAs per SM) wins while the key loop is short; from
+    // S > 256 on the <64, 8> tiling halves the per-key-tile overhead and is
+    // faster (measured: S = 128 -> <32, 4>, S = 512 -> <64, 8>).
+    // ICONNX_ATTENTION_TILE=32 or =64 forces one of them.
+    static const int forced = [] {
       const char* e = getenv("ICONNX_ATTENTION_TILE");
-      return e != nullptr && strcmp(e, "64") == 0;
+      return e == nullptr ? 0 : atoi(e);
     }();
+    const bool wide = forced == 64 || (forced != 32 && S > 256);
     dim3 grid((unsigned)((S + kTcQ - 1) / kTcQ), (unsigned)(B * nh));
     auto launch = [&](auto kern, int threads, int smem) -> int {
       ICX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));

@@ -43,7 +43,9 @@ def test_attention_reference_matches_cpu_interpreter():
     (3, 200, 256, 4, "shared"),    # ragged query and key tiles
     (2, 16, 128, 2, "none"),       # one partial tile
     (1, 1, 64, 1, "batch"),        # a single key
-    (1, 384, 768, 12, "batch"),    # three query tiles, six key tiles
+    (1, 384, 768, 12, "batch"),    # three query tiles, six key tiles (wide tiling)
+    (2, 300, 256, 4, "shared"),    # ragged tiles on the wide tiling
+    (2, 512, 768, 12, "batch"),    # the BERT-base sequence length
 ])
 def test_fused_attention_matches_float64(batch, seq, hidden, heads, mask):
     from iconnx_b200.engine import GpuGraphExecutor
