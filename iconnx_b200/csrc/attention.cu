@@ -679,8 +679,6 @@ int launch_attention_f32(cudaStream_t s, const float* q, const float* k, const f
   if (!simt) {
     ICX_REQUIRE(B * nh <= 65535, "Attention: batch x heads %lld too large", (long long)(B * nh));
     const int parts = attention_partials(B, S, nh);
-    ICX_REQUIRE(minmax == nullptr || parts <= ICX_MAX_MINMAX_PARTIALS,
-                "Attention: %d (min, max) partials exceed %d", parts, ICX_MAX_MINMAX_PARTIALS);
     int cexp;
     const bool c_pow2 = frexpf(c, &cexp) == 0.5f;
     // <32, 4> (three CTAs per SM) wins while the key loop is short; from

@@ -1074,6 +1074,7 @@ class Engine {
     }
     // producer-fused min/max for DynamicQuantizeLinear
     int slot = 0;
+    wide_parts_ = 0;
     for (int idx : order_) {
       const NodeDef& d = nodes_[idx];
       if (d.op != "DynamicQuantizeLinear" || skip_.count(idx)) continue;
@@ -1088,9 +1089,13 @@ class Engine {
         if (kv.second.out == d.in[0]) ok = true;
       for (auto& kv : attn_) {
         const FusedAttn& a = kv.second;
-        if (a.out == d.in[0] && attention_supported(a.dh, a.ld ? a.ld : a.H, a.H) &&
-            attention_partials(a.B, a.S, a.nh) <= ICX_MAX_MINMAX_PARTIALS)
+        if (a.out == d.in[0] && attention_supported(a.dh, a.ld ? a.ld : a.H, a.H)) {
           ok = true;
+          // more partials than a slot holds: they go to a wider buffer and
+          // are folded into the slot's single pair after the kernel
+          const size_t parts = (size_t)attention_partials(a.B, a.S, a.nh);
+          if (parts > (size_t)ICX_MAX_MINMAX_PARTIALS) wide_parts_ = std::max(wide_parts_, parts);
+        }
       }
       if (!ok) continue;
       x.minmax_slot = slot;
@@ -1421,6 +1426,8 @@ class Engine {
     const size_t slot_bytes = (size_t)ICX_MAX_MINMAX_PARTIALS * 8;
     slots_off_ = total;
     total += slot_bytes * (size_t)(n_slots_ + 1);
+    wide_off_ = total;
+    if (wide_parts_ > 0) total += wide_parts_ * 8 + 512;  // partials, then the folded pair
     if (total > arena_bytes_) {
       if (arena_) cudaFree(arena_);
       arena_ = nullptr;
@@ -1439,6 +1446,9 @@ class Engine {
                                     (size_t)slot * ICX_MAX_MINMAX_PARTIALS * 8);
   }
   float* dql_workspace() { return slot_ptr(n_slots_); }
+  float* wide_partials() {
+    return reinterpret_cast<float*>(static_cast<uint8_t*>(arena_) + wide_off_);
+  }
 
   // --------------------------------------------------------- step build
   int build_steps() {
@@ -1517,6 +1527,23 @@ class Engine {
       const int slot = vals_[a.out].minmax_slot;
       float* mm = slot >= 0 ? slot_ptr(slot) : nullptr;
       int* mmc = slot >= 0 ? &minmax_count_[slot] : nullptr;
+      const int parts = attention_partials(a.B, a.S, a.nh);
+      if (mm != nullptr && parts > ICX_MAX_MINMAX_PARTIALS) {
+        // (min, max) is order-independent, so folding the per-CTA partials
+        // into one pair leaves the DynamicQuantizeLinear result unchanged
+        float* wide = wide_partials();
+        float* g = wide + ((size_t)parts * 2 + 63) / 64 * 64;
+        add_step(n, "Attention", a.out, [=](cudaStream_t s) {
+          int written = 0;
+          int rc = launch_attention_f32(s, q, k, v, ld, out, at.B, at.S, at.H, at.nh, at.c, mask,
+                                        at.mask_per_batch, wide, &written);
+          if (rc == ICX_OK) rc = launch_minmax_fold(s, wide, written, g);
+          if (rc == ICX_OK) rc = launch_minmax_unfold(s, g, mm);
+          *mmc = 1;
+          return rc;
+        }, 3);
+        return ICX_OK;
+      }
       add_step(n, "Attention", a.out, [=](cudaStream_t s) {
         return launch_attention_f32(s, q, k, v, ld, out, at.B, at.S, at.H, at.nh, at.c, mask,
                                     at.mask_per_batch, mm, mmc);
@@ -1887,6 +1914,8 @@ class Engine {
   float* gdql_ = nullptr;      // (-min, max) pair [0..1] and the (min, max) partial [2..3]
   std::map<int, int> dql_mode_;
   int n_slots_ = 0;
+  size_t wide_parts_ = 0;  // largest attention partial count above a slot's room
+  size_t wide_off_ = 0;
   std::vector<int> minmax_count_;
   std::map<std::string, Prepared> prepared_;
   std::vector<void*> scratch_;

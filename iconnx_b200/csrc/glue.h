@@ -36,7 +36,8 @@ int launch_gelu(cudaStream_t s, const float* x, float* y, size_t n);
 // attention.cu
 bool attention_supported(int64_t dh, int64_t ld, int64_t H);
 // (min, max) partials of the output for the DynamicQuantizeLinear that
-// reads it when `minmax` is given (attention_partials of them).
+// reads it when `minmax` is given (attention_partials of them; the buffer
+// must hold that many pairs, which may exceed ICX_MAX_MINMAX_PARTIALS).
 int attention_partials(int64_t B, int64_t S, int64_t nh);
 int launch_attention_f32(cudaStream_t s, const float* q, const float* k, const float* v, int64_t ld,
                          float* out, int64_t B, int64_t S, int64_t H, int64_t nh, float c,

@@ -82,3 +82,28 @@ def test_fused_attention_large_scores_as_accurate_as_fp32():
     graphs.build_attention(ex, batch, seq, hidden, heads, "batch")
     e_gpu = np.max(np.abs(ex.run(inp, [out])[out] - ref))
     assert e_gpu <= 2.0 * e_cpu + 1e-6, (e_gpu, e_cpu)
+
+
+@gpu
+@pytest.mark.parametrize("batch", [2, 26])
+def test_attention_fused_minmax_feeds_dynamic_quantize(batch):
+    """DynamicQuantizeLinear on the attention output takes (min, max) from the
+    attention kernel's epilogue and runs only its quantise pass.  At batch 26
+    x 12 heads x 4 query tiles the kernel writes 1248 partials, more than a
+    DQL slot holds; they are folded into one pair first.  Either way the
+    quantised tensor, scale and zero point are bit-exact against the oracle's
+    DynamicQuantizeLinear of the same attention output."""
+    from iconnx_b200.engine import GpuGraphExecutor
+    from oracle import oracle
+    seq, hidden, heads = 512, 768, 12
+    ex = GpuGraphExecutor.new()
+    out = graphs.build_attention(ex, batch, seq, hidden, heads, "batch")
+    ex.add_node("dql", "DynamicQuantizeLinear", [out], ["y", "y_scale", "y_zp"])
+    inp = _inputs(batch, seq, hidden, "batch", 7 + batch)
+    res = ex.run(inp, [out, "y", "y_scale", "y_zp"])
+    plan = ex.plan()
+    assert any(s.startswith("DynamicQuantizeLinear(quantise)") for s in plan), plan
+    y, scale, zp = oracle.dynamic_quantize_linear(res[out])
+    np.testing.assert_array_equal(res["y"], y)
+    assert np.float32(res["y_scale"]).tobytes() == np.float32(scale).tobytes()
+    assert np.uint8(res["y_zp"]) == np.uint8(zp)
