@@ -265,7 +265,13 @@ struct AttTc {
   static constexpr int kOffScale = kOffRed + kRedFloats * 4;  // 2^(nq-1) per row, 2^(nk-1) per key
   static constexpr int kOffMask = kOffScale + (kTcQ + KT) * 4;  // additive mask of the tile
   static constexpr int kOffBar = kOffMask + KT * 4;
-  static constexpr int kSmem = kOffBar + 64 + 1024 /*align slack*/;
+  // fp32 staging of the next tile, filled by cp.async while this tile's
+  // softmax runs: V always, K too where three CTAs per SM still fit (<32, 4>;
+  // <64, 8> keeps K in registers)
+  static constexpr bool kStageK = KT == 32;
+  static constexpr int kOffRawK = kOffBar + 64;
+  static constexpr int kOffRawV = kOffRawK + (kStageK ? KT * 256 : 0);
+  static constexpr int kSmem = kOffRawV + KT * 256 + 1024 /*align slack*/;
   static constexpr uint32_t kTmemCols = 4 * KT;  // the score levels; P and O_tile reuse them
   static constexpr int kTmemPh = 0;              // P hi (after the scores are consumed)
   static constexpr int kTmemPl = KT;             // P lo
@@ -395,8 +401,10 @@ __global__ void __launch_bounds__(32 * NW, (KT == 64 ? 2 : 3))
   // (its outputs) are read only from here on
   pdl_wait();
   pdl_trigger();
-  float4 nk[A::kKLoads];
-  float nm = 0.0f;  // the tile's additive mask value for key tid (tid < 64)
+  float4 nk[A::kStageK ? 1 : A::kKLoads];  // next K tile (when not staged in shared memory)
+  float nm = 0.0f;  // the tile's additive mask value for key tid (tid < KT)
+  float* raw_k = reinterpret_cast<float*>(sm + A::kOffRawK);
+  float* raw_v = reinterpret_cast<float*>(sm + A::kOffRawV);
   auto load_k = [&](int k0) {
 #pragma unroll
     for (int i = 0; i < A::kKLoads; ++i) {
@@ -404,6 +412,18 @@ __global__ void __launch_bounds__(32 * NW, (KT == 64 ? 2 : 3))
       nk[i] = kr < S ? __ldg(reinterpret_cast<const float4*>(k + head + (size_t)kr * ld + kv_col))
                      : make_float4(0.f, 0.f, 0.f, 0.f);
     }
+  };
+  // cp.async of the tile's V (and K when staged) rows into the raw buffers,
+  // rows past S zero-filled; the mask value of key tid into nm
+  auto stage_tile = [&](int k0) {
+#pragma unroll
+    for (int i = 0; i < A::kKLoads; ++i) {
+      const int r = kv_row + kRowStep * i, kr = k0 + r;
+      const size_t src = head + (size_t)(kr < S ? kr : 0) * ld + kv_col;
+      if (A::kStageK) cp_async16(raw_k + r * 64 + kv_col, k + src, kr < S);
+      cp_async16(raw_v + r * 64 + kv_col, v + src, kr < S);
+    }
+    cp_async_commit();
     if (tid < KT) {
       const int key = k0 + tid;
       nm = key >= S ? -INFINITY : (mrow ? __ldg(mrow + key) : 0.0f);
@@ -417,7 +437,8 @@ __global__ void __launch_bounds__(32 * NW, (KT == 64 ? 2 : 3))
       vq[i] = qi < S ? __ldg(reinterpret_cast<const float4*>(q + head + (size_t)qi * ld + kv_col))
                      : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    load_k(0);
+    if (!A::kStageK) load_k(0);
+    stage_tile(0);
 #pragma unroll
     for (int i = 0; i < A::kQLoads; ++i) {
       const int r = kv_row + kRowStep * i;
@@ -441,11 +462,23 @@ __global__ void __launch_bounds__(32 * NW, (KT == 64 ? 2 : 3))
   bool ok = true;
   uint32_t phase = 0;
   for (int k0 = 0; k0 < S; k0 += KT, phase ^= 1) {
-    // 1. K slices and the mask of this tile
+    // 1. K slices, V^T hi / lo and the mask of this tile (the staged rows
+    // of every thread are visible after the wait and the barrier)
+    cp_async_wait_all();
+    __syncthreads();
 #pragma unroll
     for (int i = 0; i < A::kKLoads; ++i) {
-      const float f = slice_row_store(sm + A::kOffKs, A::kKAtom, kv_row + kRowStep * i, kv_col, nk[i]);
-      if (kv_col == 0) k_scale[kv_row + kRowStep * i] = f;
+      const int r = kv_row + kRowStep * i;
+      const float4 kx = A::kStageK ? *reinterpret_cast<const float4*>(raw_k + r * 64 + kv_col) : nk[i];
+      const float f = slice_row_store(sm + A::kOffKs, A::kKAtom, r, kv_col, kx);
+      if (kv_col == 0) k_scale[r] = f;
+    }
+#pragma unroll
+    for (int g = 0; g < A::kVKeys / 4; ++g) {
+      const int key = v_key + 4 * g;
+      const float4 vx = make_float4(raw_v[key * 64 + v_d], raw_v[(key + 1) * 64 + v_d],
+                                    raw_v[(key + 2) * 64 + v_d], raw_v[(key + 3) * 64 + v_d]);
+      split_store(sm + A::kOffVh, sm + A::kOffVl, A::kVAtom, v_d, key, vx);
     }
     if (tid < KT) m_tile[tid] = nm;
     fence_proxy_async_smem();
@@ -476,22 +509,9 @@ __global__ void __launch_bounds__(32 * NW, (KT == 64 ? 2 : 3))
       }
       mma_commit(bar_s);
     }
-    {
-      float4 nv[A::kVKeys / 4];
-#pragma unroll
-      for (int g = 0; g < A::kVKeys / 4; ++g) {
-        float x[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int vr = k0 + v_key + 4 * g + u;
-          x[u] = vr < S ? __ldg(v + head + (size_t)vr * ld + v_d) : 0.0f;
-        }
-        nv[g] = make_float4(x[0], x[1], x[2], x[3]);
-      }
-#pragma unroll
-      for (int g = 0; g < A::kVKeys / 4; ++g)
-        split_store(sm + A::kOffVh, sm + A::kOffVl, A::kVAtom, v_d, v_key + 4 * g, nv[g]);
-    }
+    // the raw buffers were consumed before the barrier: the next tile's rows
+    // stream in while this tile's scores and softmax run
+    if (k0 + KT < S) stage_tile(k0 + KT);
     ok = mbar_wait_warp(bar_s, phase, ICX_DEVICE_TIMEOUT_EPILOGUE);
     tc_fence_after();
     // 3. scores: (((acc3 / 2^24 + acc2 / 2^16) + acc1 / 2^8) + acc0), one
@@ -591,7 +611,7 @@ __global__ void __launch_bounds__(32 * NW, (KT == 64 ? 2 : 3))
       }
       mma_commit(bar_o);
     }
-    if (k0 + KT < S) load_k(k0 + KT);
+    if (!A::kStageK && k0 + KT < S) load_k(k0 + KT);
     ok = mbar_wait_warp(bar_o, phase, ICX_DEVICE_TIMEOUT_EPILOGUE);
     tc_fence_after();
     if (ok) {
@@ -607,6 +627,7 @@ __global__ void __launch_bounds__(32 * NW, (KT == 64 ? 2 : 3))
     // TMEM reads of this tile are done before the next tile's MMAs overwrite
     tc_fence_before();
   }
+  cp_async_wait_all();  // nothing in flight into shared memory at exit (early break)
   red_sum[cg * kTcQ + row] = l_part;
   ok = __syncthreads_and(ok) != 0;
   const int qi = q0 + row;
