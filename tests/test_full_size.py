@@ -91,3 +91,33 @@ def test_wide_shallow_gemm_sampled(M, K, N, gelu):
         np.testing.assert_allclose(got, oracle.gelu(ref), rtol=0, atol=1e-5)
     else:
         np.testing.assert_array_equal(got.view(np.uint32), ref.view(np.uint32))
+
+
+@pytest.mark.parametrize("M,K,N,per_col,gelu", [
+    (4000, 1552, 4064, True, False),   # ragged M / N / K, per-column scale and zero point
+    (4096, 2048, 4096, False, True),   # GELU epilogue
+])
+def test_long_k_gemm_every_row(M, K, N, per_col, gelu):
+    """Long-K (K >= 1536, deep stage ring) GEMMs with every output row
+    checked: ragged M / N / K tails, per-column scale and zero point, and the
+    GELU epilogue; bit-exact (1e-5 after GELU)."""
+    x = synth.normal((M, K), 1.0, 21)
+    w = synth.int8_uniform((K, N), 22)
+    ws = synth.uniform_f32((N,), 0.005, 0.02, 23) if per_col else np.array([0.01], np.float32)
+    bias = synth.normal((N,), 0.02, 24)
+    bz = synth.int8_uniform((N,), 25, -8, 8) if per_col else None
+    pw = ops.prepare_weight(torch.from_numpy(w).to(DEV))
+    bzt = None if bz is None else torch.from_numpy(bz).to(DEV)
+    out, y, s, z = ops.dynamic_quant_linear(torch.from_numpy(x).to(DEV), pw,
+                                            torch.from_numpy(ws).to(DEV),
+                                            torch.from_numpy(bias).to(DEV), bzt, gelu=gelu)
+    oy, os_, oz = oracle.dynamic_quantize_linear(x)
+    np.testing.assert_array_equal(y.cpu().numpy(), oy)
+    acc = oracle.matmul_integer(oy, w, np.uint8(oz), bz, threads=oracle.max_threads())
+    sc = np.float32(os_) * ws.astype(np.float32)
+    ref = (oracle.cast_i32_f32(acc) * (sc if sc.size > 1 else sc[0]) + bias).astype(np.float32)
+    got = out.cpu().numpy()
+    if gelu:
+        np.testing.assert_allclose(got, oracle.gelu(ref), rtol=0, atol=1e-5)
+    else:
+        np.testing.assert_array_equal(got.view(np.uint32), ref.view(np.uint32))
