@@ -4,7 +4,8 @@
 //
 // Replaces the reference's one-thread-per-output SIMT kernel
 // matmul_integer_u8s8_kernel (src/cuda/ops/quantize_kernels.rs:116-194) and
-// the Cast/Mul/Add/Erf launches that follow it (SURVEY call stack 3.2).
+// the Cast/Mul/Add/Erf launches that follow it (the executor's per-op dispatch,
+// src/cuda/executor/layout.rs:1034-1097 and src/cuda/executor/elementwise.rs).
 //
 // Kernel structure (one CTA per SM, persistent over output tiles):
 //   warp 0      TMA producer: 128x128-byte A tiles and BNx128-byte B tiles
