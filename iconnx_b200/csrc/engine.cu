@@ -247,9 +247,12 @@ class Engine {
 
   // Validates the inputs, (re)compiles when their shapes or the requested
   // outputs change, and queues the inputs' host->device copies on the stream.
+  // Validates the inputs, compiles the plan for their shapes when needed and,
+  // with `upload`, copies them into the plan's input slots on the compute
+  // stream.
   int stage_inputs(const std::vector<std::string>& names, const std::vector<int>& dtypes,
                    const std::vector<Shape>& shapes, const std::vector<const void*>& host,
-                   const std::vector<std::string>& outputs) {
+                   const std::vector<std::string>& outputs, bool upload = true) {
     ICX_CUDA(cudaSetDevice(device_));
     // input-shape guard (src/cuda/inference/mod.rs:441-460): declared
     // static dimensions must match; dynamic ones (<= 0) may vary.
@@ -288,7 +291,7 @@ class Engine {
         return rc;
       }
     }
-    for (size_t i = 0; i < names.size(); ++i) {
+    for (size_t i = 0; i < names.size() && upload; ++i) {
       Val& v = vals_[names[i]];
       const size_t bytes = (size_t)numel(v.shape) * dtype_size(v.dtype);
       if (bytes) ICX_CUDA(cudaMemcpyAsync(v.ptr, host[i], bytes, cudaMemcpyHostToDevice, stream_));
@@ -359,16 +362,50 @@ class Engine {
              const std::vector<Shape>& shapes, const std::vector<const void*>& host,
              const std::vector<std::string>& outputs, const std::vector<void*>& host_out,
              const std::vector<size_t>& out_bytes, int64_t* ticket) {
-    int rc = stage_inputs(names, dtypes, shapes, host, outputs);
-    if (rc) return rc;
-    rc = execute();
+    int rc = stage_inputs(names, dtypes, shapes, host, outputs, /*upload=*/false);
     if (rc) return rc;
     if (!copy_stream_) ICX_CUDA(cudaStreamCreateWithFlags(&copy_stream_, cudaStreamNonBlocking));
+    if (!upload_stream_) ICX_CUDA(cudaStreamCreateWithFlags(&upload_stream_, cudaStreamNonBlocking));
     Pending& p = pend_[next_ticket_ & 1];
     if (!p.ready) {
       ICX_CUDA(cudaEventCreateWithFlags(&p.ready, cudaEventDisableTiming));
       ICX_CUDA(cudaEventCreateWithFlags(&p.done, cudaEventDisableTiming));
+      ICX_CUDA(cudaEventCreateWithFlags(&p.in_ready, cudaEventDisableTiming));
+      ICX_CUDA(cudaEventCreateWithFlags(&p.in_free, cudaEventDisableTiming));
     }
+    // Inputs: host -> this slot's device staging on the upload stream, which
+    // overlaps the previous submission's compute (an upload on the compute
+    // stream would wait for it and then delay this plan), then one device
+    // copy per input into the plan's input slots on the compute stream.
+    if (p.in_used) ICX_CUDA(cudaStreamWaitEvent(upload_stream_, p.in_free, 0));
+    if (p.in_buf.size() < names.size()) {
+      p.in_buf.resize(names.size(), nullptr);
+      p.in_cap.resize(names.size(), 0);
+    }
+    std::vector<size_t> in_bytes(names.size());
+    for (size_t i = 0; i < names.size(); ++i) {
+      const Val& v = vals_[names[i]];
+      in_bytes[i] = (size_t)numel(v.shape) * dtype_size(v.dtype);
+      if (p.in_cap[i] < in_bytes[i]) {
+        ICX_CUDA(cudaStreamSynchronize(stream_));
+        if (p.in_buf[i]) ICX_CUDA(cudaFree(p.in_buf[i]));
+        ICX_CUDA(cudaMalloc(&p.in_buf[i], in_bytes[i]));
+        p.in_cap[i] = in_bytes[i];
+      }
+      if (in_bytes[i])
+        ICX_CUDA(cudaMemcpyAsync(p.in_buf[i], host[i], in_bytes[i], cudaMemcpyHostToDevice,
+                                 upload_stream_));
+    }
+    ICX_CUDA(cudaEventRecord(p.in_ready, upload_stream_));
+    ICX_CUDA(cudaStreamWaitEvent(stream_, p.in_ready, 0));
+    for (size_t i = 0; i < names.size(); ++i)
+      if (in_bytes[i])
+        ICX_CUDA(cudaMemcpyAsync(vals_[names[i]].ptr, p.in_buf[i], in_bytes[i],
+                                 cudaMemcpyDeviceToDevice, stream_));
+    ICX_CUDA(cudaEventRecord(p.in_free, stream_));
+    p.in_used = true;
+    rc = execute();
+    if (rc) return rc;
     if (p.busy) ICX_CUDA(cudaStreamWaitEvent(stream_, p.done, 0));  // its last download is done
     if (p.buf.size() < outputs.size()) {
       p.buf.resize(outputs.size(), nullptr);
@@ -503,6 +540,9 @@ class Engine {
     runs_ = 0;
   }
   void release() {
+    // nothing of this engine may still run on the buffers freed below
+    for (cudaStream_t st : {stream_, copy_stream_, upload_stream_})
+      if (st) cudaStreamSynchronize(st);
     drop_graph();
     if (arena_) cudaFree(arena_);
     for (auto& kv : prepared_) {
@@ -521,10 +561,14 @@ class Engine {
     if (blas_ws_) cudaFree(blas_ws_);
     for (auto& p : pend_) {
       for (void* b : p.buf) if (b) cudaFree(b);
+      for (void* b : p.in_buf) if (b) cudaFree(b);
       if (p.ready) cudaEventDestroy(p.ready);
       if (p.done) cudaEventDestroy(p.done);
+      if (p.in_ready) cudaEventDestroy(p.in_ready);
+      if (p.in_free) cudaEventDestroy(p.in_free);
     }
     if (copy_stream_) cudaStreamDestroy(copy_stream_);
+    if (upload_stream_) cudaStreamDestroy(upload_stream_);
     if (comm_) nccl_api()->comm_destroy(comm_);
     if (gdql_) cudaFree(gdql_);
     if (stream_) cudaStreamDestroy(stream_);
@@ -1904,11 +1948,17 @@ class Engine {
     std::vector<void*> buf;
     std::vector<size_t> cap;
     cudaEvent_t ready = nullptr, done = nullptr;
+    // device staging of the submission's inputs (upload stream)
+    std::vector<void*> in_buf;
+    std::vector<size_t> in_cap;
+    cudaEvent_t in_ready = nullptr, in_free = nullptr;
+    bool in_used = false;
     bool busy = false;
     int64_t ticket = -1;
   };
   Pending pend_[2];
   cudaStream_t copy_stream_ = nullptr;
+  cudaStream_t upload_stream_ = nullptr;
   int64_t next_ticket_ = 0;
   ncclComm_t comm_ = nullptr;  // global DQL (set_global_dql)
   float* gdql_ = nullptr;      // (-min, max) pair [0..1] and the (min, max) partial [2..3]
