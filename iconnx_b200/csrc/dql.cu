@@ -18,7 +18,9 @@
 // computed in f32; since |x / scale| <= 255, |t - x/scale| < 3.1e-5.  If t is
 // farther than 1e-4 from the nearest half-integer, rounding t and rounding
 // the exact quotient give the same integer, so rintf(t) is the reference's
-// result.  Otherwise (about 0.02% of random inputs, and all exact ties) the
+// result.  The vector path rounds u = fma(x, f32(1/scale), zp) instead
+// (|u - (x/scale + zp)| < 4.6e-5, zp an integer), with the same 1e-4 band.
+// Otherwise (about 0.02% of random inputs, and all exact ties) the
 // element takes the f64 division path.  Non-finite values and scales whose
 // reciprocal is not a normal f32 also take the f64 path.
 #include <mutex>
@@ -157,22 +159,26 @@ __device__ __forceinline__ uint32_t quant1(float xv, const DqlParams& p) {
 }
 
 // Four elements at once.  Common case (finite scale, no element within 1e-4
-// of a half-integer): rintf, add the zero point, clamp to [0, 255] with
-// fminf/fmaxf (NaN -> 0), and read the integer out of the float's low byte
+// of a half-integer): rintf of x * (1/scale) + zp (one FMA), clamp to
+// [0, 255] with fminf/fmaxf (NaN -> 0), and read the integer out of the float's low byte
 // after adding 2^23; byte_perm packs the four bytes.  Otherwise every
 // element takes quant1 (with its exact f64 path where needed).
 template <bool SUM>
 __device__ __forceinline__ uint32_t quant4(float4 v, const DqlParams& p, uint32_t& sum) {
   if (p.fast) {
-    const float t0 = v.x * p.inv32, t1 = v.y * p.inv32, t2 = v.z * p.inv32, t3 = v.w * p.inv32;
-    const float r0 = rintf(t0), r1 = rintf(t1), r2 = rintf(t2), r3 = rintf(t3);
-    const bool near = (fabsf(fabsf(t0 - r0) - 0.5f) <= 1e-4f) | (fabsf(fabsf(t1 - r1) - 0.5f) <= 1e-4f) |
-                      (fabsf(fabsf(t2 - r2) - 0.5f) <= 1e-4f) | (fabsf(fabsf(t3 - r3) - 0.5f) <= 1e-4f);
+    // u = x * f32(1/scale) + zp in one rounding: |u - (x/scale + zp)| <=
+    // 255 * 2^-24 + 2^-15 < 4.6e-5 (|u| < 512), so away from the 1e-4 band
+    // around half-integers rint(u) = rte(x/scale) + zp (zp is an integer)
+    const float u0 = __fmaf_rn(v.x, p.inv32, p.zpf), u1 = __fmaf_rn(v.y, p.inv32, p.zpf);
+    const float u2 = __fmaf_rn(v.z, p.inv32, p.zpf), u3 = __fmaf_rn(v.w, p.inv32, p.zpf);
+    const float r0 = rintf(u0), r1 = rintf(u1), r2 = rintf(u2), r3 = rintf(u3);
+    const bool near = (fabsf(fabsf(u0 - r0) - 0.5f) <= 1e-4f) | (fabsf(fabsf(u1 - r1) - 0.5f) <= 1e-4f) |
+                      (fabsf(fabsf(u2 - r2) - 0.5f) <= 1e-4f) | (fabsf(fabsf(u3 - r3) - 0.5f) <= 1e-4f);
     if (!near) {
-      const float q0 = fminf(fmaxf(r0 + p.zpf, 0.0f), 255.0f);
-      const float q1 = fminf(fmaxf(r1 + p.zpf, 0.0f), 255.0f);
-      const float q2 = fminf(fmaxf(r2 + p.zpf, 0.0f), 255.0f);
-      const float q3 = fminf(fmaxf(r3 + p.zpf, 0.0f), 255.0f);
+      const float q0 = fminf(fmaxf(r0, 0.0f), 255.0f);
+      const float q1 = fminf(fmaxf(r1, 0.0f), 255.0f);
+      const float q2 = fminf(fmaxf(r2, 0.0f), 255.0f);
+      const float q3 = fminf(fmaxf(r3, 0.0f), 255.0f);
       if (SUM) sum += (uint32_t)((q0 + q1) + (q2 + q3));
       const uint32_t b0 = __float_as_uint(q0 + 8388608.0f), b1 = __float_as_uint(q1 + 8388608.0f);
       const uint32_t b2 = __float_as_uint(q2 + 8388608.0f), b3 = __float_as_uint(q3 + 8388608.0f);
