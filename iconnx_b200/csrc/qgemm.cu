@@ -19,7 +19,8 @@
 //               f32 dequantisation, bias, optional GELU, global stores.
 // All mbarrier waits are bounded (common.cuh).
 //
-// Zero-point correction (exact modulo 2^32, like the reference's i32 math):
+// Zero-point correction (exact modulo 2^32; the reference's checked i32
+// arithmetic panics where this wraps, which no in-range K reaches):
 //   sum_k (a - za)(b - zb[n]) = sum_k a*b - za*colsum_b[n] - zb[n]*rowsum_a[m]
 //                               + K*za*zb[n]
 // The tensor cores compute sum_k a*b on the raw u8/s8 values.
