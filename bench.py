@@ -46,12 +46,12 @@ sys.path.insert(0, ROOT)
 METRIC = "DistilBERT-int8 seq/s at 1/2/4/8 B200; MatMulInteger int8 TOPS vs peak"
 INT8_PEAK_TOPS = 4500.0  # B200 dense int8, datasheet (no measured int8 peak on this pool)
 
-# DRAM bytes (read + write) of one launch of the roofline kernel, from the ncu
-# captures summarised in profiles/ (cold cache).  The M=4096 x 768 x 3072 GELU
-# GEMM: profiles/qgemm_gelu_ffn1_M4096_K768_N3072.md.  The sweep kernel
-# (M=65536, K=N=4096) is too large to capture under the size rule: its value is
-# the M=8192 capture (profiles/qgemm_large_M8192_K4096_N4096.md) scaled by the
-# 8x rows, which is how its traffic grows (A and the output scale with M).
+# DRAM bytes (read + write) of one launch of the roofline kernel, from one
+# ncu capture (cold cache) of `bench.py --kernel ffn1 --shape 4096,768,3072`.
+# The sweep kernel (M=65536, K=N=4096) is too large to capture under the
+# profiling size rule: its value is the M=8192 capture of
+# `bench.py --kernel gemm --shape 8192,4096,4096` scaled by the 8x rows, which
+# is how its traffic grows (A and the output scale with M).
 TRAFFIC_FFN1_M4096 = 5.575168e6 + 0.987904e6
 TRAFFIC_SWEEP_FROM_M8192 = 8 * (50.599424e6 + 81.093632e6)
 
@@ -314,6 +314,96 @@ def _ffn_gemm_probe(torch, device, M, K=768, N=3072):
         f"quant_linear_gelu M={M} K={K} N={N}"
 
 
+def _timed_launches(torch, dev, stream, launch, flush, reps=10):
+    """Median device time (ms) of single launches, each bracketed by CUDA
+    events on `stream`, with a 256 MiB L2 flush before each (outside the
+    events), after 3 untimed launches."""
+    for _ in range(3):
+        launch()
+    cur = torch.cuda.current_stream(dev)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(reps)]
+    for a, b in evs:
+        flush.fill_(1)
+        stream.wait_stream(cur)
+        with torch.cuda.stream(stream):
+            a.record(stream)
+            launch()
+            b.record(stream)
+        cur.wait_stream(stream)
+    torch.cuda.synchronize(dev)
+    return float(np.median([a.elapsed_time(b) for a, b in evs]))
+
+
+def north_star_gemms(torch, dev, flush, peaks):
+    """The fused MatMulInteger target of the north star ("fused MatMulInteger
+    at >= 60% of dense int8 tensor peak at config-4 large M") at config 4's
+    two Linear shapes (M = 64 x 512 = 32768, per-column w_scale and int8
+    weight zero points) and config 5's largest point.  Each entry: CUDA-event
+    time of one launch (L2 flushed before it), int8 TOP/s, the fraction of the
+    4.5 POPS datasheet dense int8 peak and of 2 x the measured bf16 peak, and
+    the HBM roof of the shape (algorithmic bytes at the measured copy
+    bandwidth) for shapes whose f32 output makes them memory-bound."""
+    from iconnx_b200 import ops, synth
+    stream = torch.cuda.Stream(dev)
+    bf16 = peaks.get("bf16_tflops", 1590.0)
+    hbm = peaks["hbm_gbs"]
+    cases = [
+        ("c4_ffn2", 32768, 3072, 768, True, False, False),
+        ("c4_ffn2_residual", 32768, 3072, 768, True, False, True),
+        ("c4_ffn1_gelu", 32768, 768, 3072, True, True, False),
+        ("c5_largest", 65536, 4096, 4096, False, False, False),
+    ]
+    res = {}
+    for name, M, K, N, per_col, gelu, residual in cases:
+        with torch.cuda.stream(stream):
+            # inputs drawn on the device (torch generator, seeded) with the
+            # configs' distributions: N(0,1), config 5 with 0.1% N(0,20)
+            # outliers; weights int8 uniform [-127, 127]
+            gen = torch.Generator(device=dev)
+            gen.manual_seed(0)
+            x = torch.randn((M, K), generator=gen, device=dev)
+            if name.startswith("c5"):
+                pick = torch.rand((M, K), generator=gen, device=dev) < 0.001
+                x[pick] *= 20.0
+                del pick
+            wk = torch.randint(-127, 128, (K, N), generator=gen, device=dev, dtype=torch.int8)
+            w = ops.prepare_weight(wk)
+            del wk
+            if per_col:
+                ws = torch.from_numpy(synth.uniform_f32((N,), 0.005, 0.02, 41)).to(dev)
+                bz = torch.from_numpy(synth.int8_uniform((N,), 51, -8, 8)).to(dev)
+                y, s, z, rows = ops.gpu_dynamic_quantize_linear(x, row_len=K)
+            else:
+                ws = torch.tensor([0.01], dtype=torch.float32, device=dev)
+                bz, rows = None, None
+                y, s, z = ops.gpu_dynamic_quantize_linear(x)
+            del x
+            b = torch.from_numpy(synth.normal((N,), 0.02, 2)).to(dev)
+            r = torch.randn((M, N), generator=gen, device=dev) if residual else None
+            out = torch.empty((M, N), dtype=torch.float32, device=dev)
+        torch.cuda.synchronize(dev)
+
+        def launch():
+            ops.quant_linear(y, s, z, w, ws, b, bz, rows, gelu=gelu, out=out, residual=r)
+        ms = _timed_launches(torch, dev, stream, launch, flush)
+        op = 2.0 * M * N * K
+        tops = op / (ms / 1e3) / 1e12
+        alg = M * K + N * K + 4 * M * N * (2 if residual else 1) + 4 * (M if rows is not None else 0)
+        t_hbm = alg / (hbm * 1e9) * 1e3
+        t_int8 = op / (INT8_PEAK_TOPS * 1e12) * 1e3
+        res[name] = {"M": M, "K": K, "N": N, "per_column": per_col, "gelu": gelu,
+                     "residual": residual, "ms": ms, "int8_tops": tops,
+                     "frac_of_4500_datasheet": tops / INT8_PEAK_TOPS,
+                     "frac_of_2x_measured_bf16": tops / (2 * bf16),
+                     "hbm_roof_ms": t_hbm, "int8_roof_ms": t_int8,
+                     "bound": "hbm" if t_hbm > t_int8 else "tensor",
+                     "frac_of_roof": max(t_hbm, t_int8) / ms}
+        del y, s, z, w, ws, bz, rows, b, r, out
+        torch.cuda.empty_cache()
+    return res
+
+
 class EncoderWorkload:
     """Configs 3 / 4: an int8 encoder through GpuGraphExecutor."""
 
@@ -511,6 +601,57 @@ def run_kernel_probe(args):
     print(f"kernel probe {args.kernel} {args.shape} done", file=sys.stderr)
 
 
+def device_ms(torch, dev, wl, steps, warmup, flush, barrier, clocks=None):
+    """Total device time (ms) of `steps` replays of the workload's step, each
+    bracketed by CUDA events on the stream the step runs on, with an L2 flush
+    before each (outside the events), after `warmup` untimed steps."""
+    replay, wstream = wl.make_replay()
+    cur = torch.cuda.current_stream(dev)
+    for _ in range(warmup):
+        replay()
+    barrier()
+    if clocks is not None:
+        clocks.start()
+        # keep the GPU under the same load for ~1.5 s so the 100 ms clock
+        # sampler sees the clocks of this workload (untimed, like the warm-up)
+        t_soak = time.time()
+        while time.time() - t_soak < 1.5:
+            for _ in range(10):
+                replay()
+            torch.cuda.synchronize(dev)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(steps)]
+    for s_ev, e_ev in evs:
+        flush.fill_(1)                      # L2 flush, outside the events
+        wstream.wait_stream(cur)
+        s_ev.record(wstream)
+        replay()
+        e_ev.record(wstream)
+        cur.wait_stream(wstream)
+    barrier()
+    return float(np.sum([s_ev.elapsed_time(e_ev) for s_ev, e_ev in evs]))
+
+
+def end_to_end_ms(torch, dev, wl, steps, warmup, barrier):
+    """Wall time (ms) of `steps` steps through the public API with host
+    buffers: inputs uploaded and the output downloaded every step."""
+    pipelined = hasattr(wl, "e2e_loop")
+    if pipelined:
+        wl.e2e_loop(warmup)
+    else:
+        for _ in range(warmup):
+            wl.e2e_step()
+    barrier()
+    t0 = time.perf_counter()
+    if pipelined:
+        h2d, d2h = wl.e2e_loop(steps)
+    else:
+        for _ in range(steps):
+            h2d, d2h = wl.e2e_step()
+    torch.cuda.synchronize(dev)
+    return (time.perf_counter() - t0) * 1e3, h2d, d2h, pipelined
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -519,6 +660,9 @@ def main():
     ap.add_argument("--workload", default="distilbert", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-north-star", action="store_true",
+                    help="skip the north-star GEMM shapes and the config-4 encoder that the "
+                         "default 1-GPU run measures after the headline workload")
     ap.add_argument("--global-dql", action="store_true",
                     help="encoders on N>1 GPUs: every DynamicQuantizeLinear takes (min, max) over "
                          "all ranks (8-byte NCCL all-reduce), matching one executor over the "
@@ -577,32 +721,9 @@ def main():
         torch.cuda.synchronize(dev)
 
     # ---- device-resident timing (value)
-    replay, wstream = wl.make_replay()
-    cur = torch.cuda.current_stream(dev)
-    for _ in range(args.warmup):
-        replay()
-    barrier()
     clocks = ClockSampler(local)
-    clocks.start()
-    # keep the GPU under the same load for ~1.5 s so the 100 ms clock sampler
-    # sees the clocks of this workload (untimed, like the warm-up)
-    t_soak = time.time()
-    while time.time() - t_soak < 1.5:
-        for _ in range(10):
-            replay()
-        torch.cuda.synchronize(dev)
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-           for _ in range(args.steps)]
-    for s_ev, e_ev in evs:
-        flush.fill_(1)                      # L2 flush, outside the events
-        wstream.wait_stream(cur)
-        s_ev.record(wstream)
-        replay()
-        e_ev.record(wstream)
-        cur.wait_stream(wstream)
-    barrier()
+    total_ms = device_ms(torch, dev, wl, args.steps, args.warmup, flush, barrier, clocks)
     clk = clocks.stop()
-    total_ms = float(np.sum([s_ev.elapsed_time(e_ev) for s_ev, e_ev in evs]))
     t = torch.tensor([total_ms], device=dev)
     if pg is not None:
         pg.all_reduce(t, op=pg.ReduceOp.MAX)
@@ -610,44 +731,17 @@ def main():
     value = wl.units_per_step * world * args.steps / (total_ms / 1e3)
 
     # ---- end-to-end through the public API, host buffers (e2e)
-    pipelined = hasattr(wl, "e2e_loop")
-    if pipelined:
-        wl.e2e_loop(args.warmup)
-    else:
-        for _ in range(args.warmup):
-            wl.e2e_step()
-    barrier()
-    t0 = time.perf_counter()
-    if pipelined:
-        h2d, d2h = wl.e2e_loop(args.steps)
-    else:
-        for _ in range(args.steps):
-            h2d, d2h = wl.e2e_step()
-    torch.cuda.synchronize(dev)
-    e2e_ms = (time.perf_counter() - t0) * 1e3
+    e2e_ms, h2d, d2h, pipelined = end_to_end_ms(torch, dev, wl, args.steps, args.warmup, barrier)
     t = torch.tensor([e2e_ms], device=dev)
     if pg is not None:
         pg.all_reduce(t, op=pg.ReduceOp.MAX)
     e2e_ms = float(t.item())
     e2e_value = wl.units_per_step * world * args.steps / (e2e_ms / 1e3)
 
-    # ---- roofline of the dominant kernel (fused GEMM), back-to-back launches
+    # ---- roofline of the dominant kernel (fused GEMM): single launches,
+    # CUDA events on the launching stream, L2 flushed before each
     launch, ops_count, bytes_alg, kdesc = wl.gemm_probe()
-    reps = 20
-    for _ in range(3):
-        launch()
-    gk = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(gk):
-        for _ in range(reps):
-            launch()
-    gk.replay()
-    torch.cuda.synchronize(dev)
-    ks, ke = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    ks.record(stream)
-    gk.replay()
-    ke.record(stream)
-    torch.cuda.synchronize(dev)
-    k_ms = ks.elapsed_time(ke) / reps
+    k_ms = _timed_launches(torch, dev, torch.cuda.Stream(dev), launch, flush, reps=20)
     peaks, peak_kind = load_peaks()
     tops = ops_count / (k_ms / 1e3) / 1e12
     gbs = bytes_alg / (k_ms / 1e3) / 1e9
@@ -693,10 +787,32 @@ def main():
             line["config"]["parallelism"] = (f"batch-shard x{world}, global DynamicQuantizeLinear "
                                              "(8-byte NCCL MAX all-reduce per DQL)")
         line["int8_gemm_tops_in_step"] = wl.gemm_ops / (total_ms / args.steps / 1e3) / 1e12
+    if world == 1 and args.workload == "distilbert" and not args.no_north_star:
+        # the north star's other targets, measured in the same run: the fused
+        # GEMM at config 4's / config 5's large-M shapes, and config 4's
+        # encoder (BERT-base, batch 64 x seq 512) on device and end to end
+        ns_clocks = ClockSampler(local)
+        ns_clocks.start()
+        gemms = north_star_gemms(torch, dev, flush, peaks)
+        c4 = WORKLOADS["bert"](dev)
+        c4_steps = max(3, min(args.steps, 10))
+        c4_ms = device_ms(torch, dev, c4, c4_steps, args.warmup, flush, barrier)
+        c4_e2e, _, _, _ = end_to_end_ms(torch, dev, c4, c4_steps, args.warmup, barrier)
+        line["north_star"] = {
+            "fused_gemm": gemms,
+            "config4_bert_base": {"seq_per_s": c4.units_per_step * c4_steps / (c4_ms / 1e3),
+                                  "e2e_seq_per_s": c4.units_per_step * c4_steps / (c4_e2e / 1e3),
+                                  "ms_per_step": c4_ms / c4_steps, "batch": c4.batch,
+                                  "seq_len": c4.seq, "steps": c4_steps,
+                                  "int8_gemm_tops_in_step": c4.gemm_ops / (c4_ms / c4_steps / 1e3) / 1e12},
+            "clocks": ns_clocks.stop()}
+        del c4
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         from oracle import oracle
         ncores, model = cpu_info()
-        v, sample = wl.cpu_sample(1)
+        from threadpoolctl import threadpool_limits
+        with threadpool_limits(limits=1):   # numpy's BLAS too: one core
+            v, sample = wl.cpu_sample(1)
         line["cpu_baseline"] = {"value": v, "unit": wl.unit, "cores": 1, "kind": "port",
                                 "sample": sample + f"; host {ncores} cores, {model}"}
     if rank == 0:

@@ -55,6 +55,11 @@ PROTOTYPES = {
     "icx_engine_replay": (_i, [_vp]),
     "icx_engine_profile": (ctypes.c_char_p, [_vp]),
     "icx_engine_stream": (_vp, [_vp]),
+    "icx_engine_step_count": (_i, [_vp]),
+    "icx_engine_step_info": (ctypes.c_char_p, [_vp, _i]),
+    "icx_engine_run_step": (_i, [_vp, _i]),
+    "icx_engine_value_info": (_i, [_vp, ctypes.c_char_p, _vp, _vp, _vp]),
+    "icx_engine_value_copy": (_i, [_vp, ctypes.c_char_p, _vp, _sz]),
 }
 
 _lib = None

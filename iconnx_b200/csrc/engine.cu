@@ -163,6 +163,9 @@ struct FusedAttn {
 struct Step {
   std::string node, op, out;
   std::function<int(cudaStream_t)> fn;
+  // "key=value;..." naming the values the step reads and writes (the
+  // per-step debug interface, icx_engine_step_info)
+  std::string info;
 };
 
 // NCCL, loaded on first use (the library has no link-time dependency on it):
@@ -527,6 +530,49 @@ class Engine {
   }
   int kernel_launches() const { return launches_per_run_; }
   cudaStream_t stream() const { return stream_; }
+
+  // ---- per-step debug interface (stage-by-stage parity of a fused plan)
+  int step_count() const { return compiled_ ? (int)steps_.size() : 0; }
+  const Step* step(int i) const {
+    return compiled_ && i >= 0 && i < (int)steps_.size() ? &steps_[(size_t)i] : nullptr;
+  }
+  // Runs plan step i alone, eagerly, and waits for it.  Steps must be run in
+  // plan order after a run (a step reads what the earlier steps wrote, and
+  // the arena reuses a slot once its last reader has run).
+  int run_step(int i) {
+    ICX_REQUIRE(step(i) != nullptr, "run_step: no step %d in the compiled plan", i);
+    ICX_CUDA(cudaSetDevice(device_));
+    int rc = steps_[(size_t)i].fn(stream_);
+    if (rc) return rc;
+    ICX_CUDA(cudaStreamSynchronize(stream_));
+    return check_err_flag();
+  }
+  // Any value the plan materialises (not only requested outputs); the data
+  // is what its arena slot holds now.
+  int value_info(const std::string& name, int* dtype, int* rank, int64_t* dims) {
+    auto it = vals_.find(name);
+    if (!compiled_ || it == vals_.end() || !resolve(name)) {
+      set_error("value '%s' is not materialised by the compiled plan", name.c_str());
+      return ICX_ERR_NOT_FOUND;
+    }
+    *dtype = it->second.dtype;
+    *rank = (int)it->second.shape.size();
+    for (int d = 0; d < *rank && d < kMaxRank; ++d) dims[d] = it->second.shape[d];
+    return ICX_OK;
+  }
+  int value_copy(const std::string& name, void* host, size_t bytes) {
+    int dt, rk;
+    int64_t dims[kMaxRank];
+    int rc = value_info(name, &dt, &rk, dims);
+    if (rc) return rc;
+    const Val& v = vals_[name];
+    const size_t need = (size_t)numel(v.shape) * dtype_size(v.dtype);
+    ICX_REQUIRE(bytes >= need, "value '%s': buffer %zu < %zu bytes", name.c_str(), bytes, need);
+    ICX_CUDA(cudaSetDevice(device_));
+    ICX_CUDA(cudaStreamSynchronize(stream_));
+    if (need) ICX_CUDA(cudaMemcpy(host, resolve(name), need, cudaMemcpyDeviceToHost));
+    return ICX_OK;
+  }
 
  private:
   // ------------------------------------------------------------ lifecycle
@@ -1512,7 +1558,11 @@ class Engine {
 
   void add_step(const NodeDef& n, const std::string& op, const std::string& out,
                 std::function<int(cudaStream_t)> fn, int launches) {
-    steps_.push_back({n.name, op, out, std::move(fn)});
+    std::string info;
+    for (size_t k = 0; k < n.in.size(); ++k) info += (k ? "," : "in=") + n.in[k];
+    info += ";outs=";
+    for (size_t k = 0; k < n.out.size(); ++k) info += (k ? "," : "") + n.out[k];
+    steps_.push_back({n.name, op, out, std::move(fn), info});
     launches_per_run_ += launches;
   }
 
@@ -1551,6 +1601,21 @@ class Engine {
                               (size_t)M, (size_t)K, (size_t)pw.N, wsp, ws_pc, bzp, bz_pc, bp,
                               gelu ? 1 : 0, res, out, mm, mmc);
     }, 1);
+    // the weights of the step by their initializer names (merged: one
+    // '|'-separated entry per part, in column order)
+    std::string w, wsn, bzn, bn;
+    const std::vector<FusedQL> single{f};
+    const std::vector<FusedQL>& parts = merged ? f.parts : single;
+    for (size_t k = 0; k < parts.size(); ++k) {
+      const char* sep = k ? "|" : "";
+      w += sep + parts[k].w;
+      wsn += sep + parts[k].ws;
+      bzn += sep + parts[k].bz;
+      bn += sep + parts[k].bias;
+    }
+    steps_.back().info = "q=" + f.q + ";s=" + f.s + ";z=" + f.z + ";w=" + w + ";ws=" + wsn +
+                         ";bz=" + bzn + ";bias=" + bn + ";residual=" + f.residual +
+                         ";gelu=" + (gelu ? "1" : "0") + ";out=" + f.out;
     return ICX_OK;
   }
 
@@ -1558,7 +1623,23 @@ class Engine {
   // Q, K, V in place from [B, S, H] (head h is the column block h*dh) and
   // write the context straight back into [B, S, H]; between them one kernel
   // applies Div(c), Add(mask) and Softmax with the rounding of those ops.
+  static std::string attention_info(const FusedAttn& a) {
+    char buf[256];
+    snprintf(buf, sizeof(buf), ";ld=%lld;off_q=%lld;off_k=%lld;off_v=%lld;c=%.9g;B=%lld;S=%lld;H=%lld;nh=%lld",
+             (long long)(a.ld ? a.ld : a.H), (long long)a.off_q, (long long)a.off_k,
+             (long long)a.off_v, (double)a.c, (long long)a.B, (long long)a.S, (long long)a.H,
+             (long long)a.nh);
+    return "q=" + a.q + ";k=" + a.k + ";v=" + a.v + ";mask=" + a.mask +
+           ";mask_per_batch=" + (a.mask_per_batch ? "1" : "0") + buf + ";out=" + a.out;
+  }
+
   int step_attention(int idx, const FusedAttn& a) {
+    const int rc = step_attention_impl(idx, a);
+    if (rc == ICX_OK) steps_.back().info = attention_info(a);
+    return rc;
+  }
+
+  int step_attention_impl(int idx, const FusedAttn& a) {
     const NodeDef& n = nodes_[idx];
     if (attention_supported(a.dh, a.ld ? a.ld : a.H, a.H)) {
       const float* q = static_cast<const float*>(resolve(a.q)) + a.off_q;
@@ -2187,6 +2268,31 @@ extern "C" int icx_engine_replay(icx_engine* h) {
 }
 
 extern "C" void* icx_engine_stream(icx_engine* h) { return h ? (void*)h->e->stream() : nullptr; }
+
+extern "C" int icx_engine_step_count(icx_engine* h) { return h ? h->e->step_count() : 0; }
+
+extern "C" const char* icx_engine_step_info(icx_engine* h, int i) {
+  const icx::Step* st = h ? h->e->step(i) : nullptr;
+  if (!st) return nullptr;
+  h->plan = st->op + "\t" + st->node + "\t" + st->out + "\t" + st->info;
+  return h->plan.c_str();
+}
+
+extern "C" int icx_engine_run_step(icx_engine* h, int i) {
+  ICX_REQUIRE(h, "run_step: null engine");
+  return h->e->run_step(i);
+}
+
+extern "C" int icx_engine_value_info(icx_engine* h, const char* name, int* dtype, int* rank,
+                                     int64_t* dims) {
+  ICX_REQUIRE(h && name && dtype && rank && dims, "value_info: bad arguments");
+  return h->e->value_info(name, dtype, rank, dims);
+}
+
+extern "C" int icx_engine_value_copy(icx_engine* h, const char* name, void* host, size_t bytes) {
+  ICX_REQUIRE(h && name && host, "value_copy: bad arguments");
+  return h->e->value_copy(name, host, bytes);
+}
 
 extern "C" const char* icx_engine_profile(icx_engine* h) {
   if (!h) return nullptr;

@@ -94,37 +94,52 @@ __device__ __forceinline__ float gelu_erf(float x) {
   return u >= 0.0f ? x - xq : xq;
 }
 
-constexpr int kEpiWarps = 8;                       // 2 per TMEM lane quadrant
-constexpr int kThreads = 64 + 32 * kEpiWarps;        // producer + MMA + epilogue
 constexpr int kStageOutBytes = 32 * 32 * 4;          // one warp's 32x32 output box
+
+// Warps: 0 TMA producer, 1 MMA issuer, 2 .. 2+EW-1 epilogue (EW / 4 per TMEM
+// lane quadrant).
+template <int EW>
+constexpr int gemm_threads() { return 64 + 32 * EW; }
 
 // DEEP (K >= 1536): the main loop dominates, so keep a deep stage ring and
 // read per-column operands from global memory (L1-prefetched).  Otherwise
-// one stage fewer pays for staging those operands in shared memory, where the
-// epilogue (the bottleneck at small K) reads them with broadcast loads.
-template <int BN, bool DEEP = false>
+// one stage fewer pays for staging each chunk's column operands in a per-warp
+// shared-memory slice, where the epilogue (the bottleneck at small K) reads
+// them with broadcast loads, and for double-buffered output staging.
+template <int BN, bool DEEP, int EW>
 struct Cfg {
-  static constexpr int kStages = BN == 256 ? (DEEP ? 4 : 3) : BN == 192 ? 4 : (DEEP ? 6 : 5);
+  // (16 epilogue warps take one stage more for their staging boxes)
+  static constexpr int kStages = BN == 256 ? (DEEP ? 4 : 3)
+                                 : BN == 192 ? (EW == 16 ? 3 : 4)
+                                             : (DEEP ? 6 : (EW == 16 ? 4 : 5));
   static constexpr int kABytes = kBM * kBK;
   static constexpr int kBBytes = BN * kBK;
   static constexpr int kStageBytes = kABytes + kBBytes;
   // two accumulators of BN columns; the allocation is a power of two
   static constexpr int kTmemCols = BN == 192 ? 512 : 2 * BN;
   static constexpr int kOutOffset = kStages * kStageBytes;
-  // per-tile column operands (colsum, a_scale*w_scale, bias), double-buffered
-  static constexpr int kParamOffset = kOutOffset + kEpiWarps * kStageOutBytes;
-  static constexpr int kParamBytes = DEEP ? 0 : 2 * 3 * BN * 4;
-  static constexpr int kBarOffset = kParamOffset + kParamBytes;
-  // barriers (2*stages + 4) * 8 B, the TMEM slot, 8 (min,max) pairs
-  static constexpr int kSmemBytes = kBarOffset + 512 + 1024 /*align slack*/;
-  // barriers, TMEM slot, (min, max) reduction slots, residual-load barriers
-  static_assert((2 * kStages + 4) * 8 + 8 + kEpiWarps * 8 <= 256, "barrier area");
+  // per-warp column operands of one 32-column chunk: colsum, scale, bias, b_zp
+  static constexpr int kOpWarpBytes = DEEP ? 0 : 4 * 32 * 4;
+  static constexpr int kBarBytes = 1024;
+  static constexpr int kFixed = kOutOffset + EW * kOpWarpBytes + kBarBytes + 1024 /*align slack*/;
+  // two output staging boxes per warp when they fit (a warp fills one while
+  // the TMA store of the other drains)
+  static constexpr int kOutBufs = kFixed + 2 * EW * kStageOutBytes <= 227 * 1024 ? 2 : 1;
+  static constexpr int kOpOffset = kOutOffset + kOutBufs * EW * kStageOutBytes;
+  static constexpr int kBarOffset = kOpOffset + EW * kOpWarpBytes;
+  static constexpr int kSmemBytes = kBarOffset + kBarBytes + 1024;
+  // barrier area: full/empty/tfull/tempty at +0, TMEM slot at +192,
+  // per-warp (min, max) slots at +256, per-warp residual barriers at +512
+  static_assert((2 * kStages + 4) * 8 <= 192, "barrier area");
+  static_assert(EW * 8 <= 256, "per-warp slots");
+  static_assert(EW % 4 == 0, "whole warps per TMEM lane quadrant");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory");
 };
 
 // Named barrier among the epilogue warps only.
+template <int EW>
 __device__ __forceinline__ void epi_sync() {
-  asm volatile("bar.sync 1, %0;" ::"n"(32 * kEpiWarps) : "memory");
+  asm volatile("bar.sync 1, %0;" ::"n"(32 * EW) : "memory");
 }
 
 // 2-D TMA store shared -> global of one 32x32 box (tracked by bulk groups).
@@ -141,6 +156,11 @@ __device__ __forceinline__ void bulk_commit() {
 }
 __device__ __forceinline__ void bulk_wait_read0() {
   asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// Waits until at most N bulk groups of this thread still read shared memory.
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
 }
 __device__ __forceinline__ void bulk_wait0() {
   asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
@@ -256,15 +276,15 @@ __device__ __forceinline__ float4 ld4f(const float* p, int n, int N, bool vec) {
                      n + 3 < N ? p[n + 3] : 0.f);
 }
 
-template <int BN, int EPI, bool HAS_BZ, bool HAS_BIAS, bool DEEP>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int BN, int EPI, bool HAS_BZ, bool HAS_BIAS, bool DEEP, int EW>
+__global__ void __launch_bounds__(gemm_threads<EW>(), 1)
     qgemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA,
                          const __grid_constant__ CUtensorMap tmB,
                          const __grid_constant__ CUtensorMap tmOut,
                          const __grid_constant__ CUtensorMap tmRes,
                          const GemmArgs args, uint32_t idesc, int tma_store, int vec_cols,
                          int tma_res) {
-  using C = Cfg<BN, DEEP>;
+  using C = Cfg<BN, DEEP, EW>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -276,9 +296,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* empty = bars + C::kStages;
   uint64_t* tfull = bars + 2 * C::kStages;
   uint64_t* tempty = tfull + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kBarOffset + 192);
+  float2* red = reinterpret_cast<float2*>(smem + C::kBarOffset + 256);
   // residual tile barriers, one per epilogue warp
-  uint64_t* rbar = reinterpret_cast<uint64_t*>(smem + C::kBarOffset + 256);
+  uint64_t* rbar = reinterpret_cast<uint64_t*>(smem + C::kBarOffset + 512);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -295,9 +316,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], kEpiWarps);
+      mbar_init(&tempty[a], EW);
     }
-    for (int w = 0; w < kEpiWarps; ++w) mbar_init(&rbar[w], 1);
+    for (int w = 0; w < EW; ++w) mbar_init(&rbar[w], 1);
     fence_barrier_init();
     fence_proxy_async_smem();
   }
@@ -384,11 +405,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ----------------------------------------------------------- epilogue
-    const int e = warp - 2;                       // 0..kEpiWarps-1
+    // Warp e owns TMEM lane quadrant (warp & 3) and the 32-column chunks
+    // part, part + kParts, ... of every tile.  Per chunk: the column
+    // operands are staged in this warp's own shared slice (no barrier with
+    // other warps), the next chunk's tcgen05.ld is issued before this
+    // chunk's math so the TMEM read overlaps it, and the accumulator is
+    // handed back to the MMA warp as soon as its last chunk is in registers.
+    const int e = warp - 2;                       // 0..EW-1
     const int quad = warp & 3;                    // TMEM lanes [32*quad, 32*quad+32)
-    const int part = e >> 2;                      // which chunks of the quadrant
-    constexpr int kParts = kEpiWarps / 4;
-    uint8_t* stage_out = sOut + e * kStageOutBytes;
+    const int part = e >> 2;
+    constexpr int kParts = EW / 4;
+    constexpr int kChunks = BN / 32;
+    // two chunk register buffers when the register budget allows it
+    constexpr bool kDoubleBuffer = EW <= 8;
     const uint32_t za = args.a_zp ? (uint32_t)ld_zp(args.a_zp, args.a_zp_signed, 0) : 0u;
     float a_scale = 0.0f, sc_scalar = 0.0f;
     if (EPI != kEpiS32) {
@@ -399,13 +428,46 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool bz_per_col = args.b_zp_per_col != 0;
     const int32_t bz_scalar = HAS_BZ ? ld_zp(args.b_zp, args.b_zp_signed, 0) : 0;
     const bool vec = vec_cols != 0;
+    // this warp's operand slice: colsum, scale, bias, b_zp of one chunk
+    int32_t* op_cs = reinterpret_cast<int32_t*>(smem + C::kOpOffset + e * C::kOpWarpBytes);
+    float* op_sc = reinterpret_cast<float*>(op_cs + 32);
+    float* op_bi = op_sc + 32;
+    int32_t* op_bz = reinterpret_cast<int32_t*>(op_bi + 32);
     int acc = 0;
     uint32_t acc_phase = 0;
     bool ok = true;  // false once a bounded wait gave up: skip work
     const bool track = (EPI != kEpiS32) && args.minmax != nullptr;
     float run_mn = 0.0f, run_mx = 0.0f;  // the DynamicQuantizeLinear seed
     uint32_t rphase = 0;                 // parity of this warp's residual barrier
-    int tile_iter = 0;                   // selects the column-operand buffer
+    int obuf = 0;                        // output staging box in use
+
+    // column operands of column n for this lane (zero past N)
+    int32_t p_cs = 0, p_bz = 0;
+    float p_sc = 0.0f, p_bi = 0.0f;
+    auto fetch_ops = [&](int nb) {
+      if (DEEP) return;
+      const int n = nb + lane;
+      p_cs = 0;
+      p_sc = sc_scalar;
+      p_bi = 0.0f;
+      p_bz = bz_scalar;
+      if (n < N) {
+        p_cs = __ldg(args.colsum + n);
+        if (EPI != kEpiS32 && sc_per_col) p_sc = __ldg(args.w_scale + n);
+        if (EPI != kEpiS32 && HAS_BIAS) p_bi = __ldg(args.bias + n);
+        if (HAS_BZ && bz_per_col) p_bz = ld_zp(args.b_zp, args.b_zp_signed, n);
+      }
+    };
+    auto stage_ops = [&]() {
+      if (DEEP) return;
+      __syncwarp();  // every lane is done with the previous chunk's slice
+      op_cs[lane] = p_cs;
+      op_sc[lane] = (EPI != kEpiS32 && sc_per_col) ? __fmul_rn(a_scale, p_sc) : p_sc;
+      op_bi[lane] = p_bi;
+      op_bz[lane] = p_bz;
+      __syncwarp();
+    };
+
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
       const int m0 = (t / num_n) * kBM;
       const int n0 = (t % num_n) * BN;
@@ -413,11 +475,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int m = mrow0 + lane;
       uint32_t kza_rs = 0;
       if (HAS_BZ) kza_rs = (uint32_t)K * za - ((m < M) ? (uint32_t)args.rowsum[m] : 0u);
-      // stage this tile's per-column operands in shared memory while the MMA
-      // runs (double-buffered by tile parity; one epilogue barrier per tile)
-      int32_t* p_cs = reinterpret_cast<int32_t*>(smem + C::kParamOffset) + (tile_iter & 1) * 3 * BN;
-      float* p_sc = reinterpret_cast<float*>(p_cs + BN);
-      float* p_bi = p_sc + BN;
+      // chunks of this tile that hold columns < N
+      const int nvalid = min(kChunks, (N - n0 + 31) / 32);
       if (DEEP) {
         // per-column operands come from global memory: pull them into L1
         const int et = threadIdx.x - 64;
@@ -430,74 +489,57 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      for (int j = threadIdx.x - 64; !DEEP && j < BN; j += 32 * kEpiWarps) {
-        const int n = n0 + j;
-        int32_t cs = 0;
-        float sc = sc_scalar, bi = 0.0f;
-        if (n < N) {
-          cs = __ldg(args.colsum + n);
-          if (EPI != kEpiS32 && sc_per_col) sc = __fmul_rn(a_scale, __ldg(args.w_scale + n));
-          if (EPI != kEpiS32 && HAS_BIAS) bi = __ldg(args.bias + n);
-        }
-        p_cs[j] = cs;
-        p_sc[j] = sc;
-        p_bi[j] = bi;
-      }
-      if (!DEEP) epi_sync();
-      ++tile_iter;
+      int c = part;
+      if (c < nvalid) fetch_ops(n0 + c * 32);   // loads in flight during the wait
       if (ok) ok = mbar_wait_warp(&tfull[acc], acc_phase, ICX_DEVICE_TIMEOUT_EPILOGUE);
       tc_fence_after();
       const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
-#pragma unroll 1
-      for (int c = part; c < BN / 32 && ok; c += kParts) {
-        const int nb = n0 + c * 32;
-        if (nb >= N) break;  // warp-uniform
-        const bool fast = (DEEP ? vec : true) && (nb + 32 <= N) && !(HAS_BZ && bz_per_col);
+      bool released = false;
+      auto release = [&]() {
+        // the accumulator's columns this warp reads are all in registers
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[acc]);
+        released = true;
+      };
+
+      // One chunk: zero-point correction, dequantisation [+ GELU]
+      // [+ residual], (min, max), store.  r holds the chunk's accumulators.
+      auto process = [&](uint32_t (&r)[32], int cc) {
+        const int nb = n0 + cc * 32;
+        uint8_t* stage_out = sOut + (obuf * EW + e) * kStageOutBytes;
         const bool res_tma = EPI == kEpiF32 && tma_res && mrow0 < M;
-        if (res_tma && lane == 0) {
-          // residual box -> this warp's staging buffer, overlapped with the math
-          bulk_wait_read0();
-          mbar_arrive_expect_tx(&rbar[e], kStageOutBytes);
-          tma_load_2d(stage_out, &tmRes, &rbar[e], nb, mrow0);
-        }
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(t_row + (uint32_t)(c * 32), r);
-        tmem_ld_wait();
+        const bool fast = DEEP ? (vec && (nb + 32 <= N) && !(HAS_BZ && bz_per_col)) : true;
         if (fast) {
-          // whole chunk in range, 16-byte aligned operand vectors
-          const int4* cs4 = reinterpret_cast<const int4*>(p_cs + c * 32);
-          const float4* sc4 = reinterpret_cast<const float4*>(p_sc + c * 32);
-          const float4* bi4 = reinterpret_cast<const float4*>(p_bi + c * 32);
-          if (DEEP) {
-            cs4 = reinterpret_cast<const int4*>(args.colsum + nb);
-            sc4 = reinterpret_cast<const float4*>(args.w_scale + nb);
-            bi4 = reinterpret_cast<const float4*>(args.bias + nb);
-          }
 #pragma unroll
           for (int q = 0; q < 8; ++q) {
-            const int4 cs = DEEP ? __ldg(cs4 + q) : cs4[q];
+            int4 cs;
             float4 sc = make_float4(sc_scalar, sc_scalar, sc_scalar, sc_scalar);
-            if (EPI != kEpiS32 && sc_per_col) {
-              if (DEEP) {
-                const float4 w = __ldg(sc4 + q);
+            float4 bi = make_float4(0.f, 0.f, 0.f, 0.f);
+            int4 bz = make_int4(bz_scalar, bz_scalar, bz_scalar, bz_scalar);
+            if (DEEP) {
+              cs = __ldg(reinterpret_cast<const int4*>(args.colsum + nb) + q);
+              if (EPI != kEpiS32 && sc_per_col) {
+                const float4 w = __ldg(reinterpret_cast<const float4*>(args.w_scale + nb) + q);
                 sc = make_float4(__fmul_rn(a_scale, w.x), __fmul_rn(a_scale, w.y),
                                  __fmul_rn(a_scale, w.z), __fmul_rn(a_scale, w.w));
-              } else {
-                sc = sc4[q];
               }
+              if (EPI != kEpiS32 && HAS_BIAS) bi = __ldg(reinterpret_cast<const float4*>(args.bias + nb) + q);
+            } else {
+              cs = reinterpret_cast<const int4*>(op_cs)[q];
+              if (EPI != kEpiS32 && sc_per_col) sc = reinterpret_cast<const float4*>(op_sc)[q];
+              if (EPI != kEpiS32 && HAS_BIAS) bi = reinterpret_cast<const float4*>(op_bi)[q];
+              if (HAS_BZ && bz_per_col) bz = reinterpret_cast<const int4*>(op_bz)[q];
             }
-            float4 bi = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (EPI != kEpiS32 && HAS_BIAS) bi = DEEP ? __ldg(bi4 + q) : bi4[q];
             int32_t v0 = (int32_t)(r[4 * q + 0] - za * (uint32_t)cs.x);
             int32_t v1 = (int32_t)(r[4 * q + 1] - za * (uint32_t)cs.y);
             int32_t v2 = (int32_t)(r[4 * q + 2] - za * (uint32_t)cs.z);
             int32_t v3 = (int32_t)(r[4 * q + 3] - za * (uint32_t)cs.w);
             if (HAS_BZ) {
-              const uint32_t kb = kza_rs * (uint32_t)bz_scalar;
-              v0 = (int32_t)((uint32_t)v0 + kb);
-              v1 = (int32_t)((uint32_t)v1 + kb);
-              v2 = (int32_t)((uint32_t)v2 + kb);
-              v3 = (int32_t)((uint32_t)v3 + kb);
+              v0 = (int32_t)((uint32_t)v0 + kza_rs * (uint32_t)bz.x);
+              v1 = (int32_t)((uint32_t)v1 + kza_rs * (uint32_t)bz.y);
+              v2 = (int32_t)((uint32_t)v2 + kza_rs * (uint32_t)bz.z);
+              v3 = (int32_t)((uint32_t)v3 + kza_rs * (uint32_t)bz.w);
             }
             finish2<EPI, HAS_BIAS>(v0, v1, sc.x, sc.y, bi.x, bi.y, r[4 * q + 0], r[4 * q + 1]);
             finish2<EPI, HAS_BIAS>(v2, v3, sc.z, sc.w, bi.z, bi.w, r[4 * q + 2], r[4 * q + 3]);
@@ -538,6 +580,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (res_tma) {
           // residual Add(out, r) from the swizzled staging copy of the box
+          // (its TMA load was issued before this chunk's accumulator wait)
           if (!mbar_wait_warp(&rbar[e], rphase, ICX_DEVICE_TIMEOUT_EPILOGUE)) ok = false;
           rphase ^= 1;
           const uint8_t* rrow = stage_out + lane * 128;
@@ -585,8 +628,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (tma_store) {
           if (mrow0 < M) {
-            // the previous box of this warp must have been read out of smem
-            if (lane == 0 && !res_tma) bulk_wait_read0();
+            // this box's previous store (kOutBufs chunks ago) must have been
+            // read out of shared memory (the residual path waited already)
+            if (lane == 0 && !res_tma) bulk_wait_read<C::kOutBufs - 1>();
             __syncwarp();
             uint8_t* row = stage_out + lane * 128;
 #pragma unroll
@@ -599,6 +643,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               tma_store_2d(&tmOut, stage_out, nb, mrow0);
               bulk_commit();
             }
+            if (C::kOutBufs == 2) obuf ^= 1;
           }
         } else if (m < M) {
           uint32_t* orow = static_cast<uint32_t*>(args.out) + (size_t)m * N + nb;
@@ -606,27 +651,86 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int j = 0; j < 32; ++j)
             if (nb + j < N) orow[j] = r[j];
         }
+      };
+      // residual box of chunk cc -> the staging box it will be stored from
+      auto residual_load = [&](int cc) {
+        if (EPI == kEpiF32 && tma_res && mrow0 < M && lane == 0) {
+          bulk_wait_read<C::kOutBufs - 1>();
+          uint8_t* stage_out = sOut + (obuf * EW + e) * kStageOutBytes;
+          mbar_arrive_expect_tx(&rbar[e], kStageOutBytes);
+          tma_load_2d(stage_out, &tmRes, &rbar[e], n0 + cc * 32, mrow0);
+        }
+      };
+
+      if (kDoubleBuffer) {
+        uint32_t ra[32], rb[32];
+        if (ok && c < nvalid) {
+          tmem_ld_32x32b_x32(t_row + (uint32_t)(c * 32), ra);
+          // chunk pairs (ra, rb): the load of the next chunk is in flight
+          // while the current one is processed
+          while (true) {
+            stage_ops();
+            residual_load(c);
+            tmem_ld_wait_regs(ra);
+            int cn = c + kParts;
+            bool more = ok && cn < nvalid;
+            if (more) {
+              tmem_ld_32x32b_x32(t_row + (uint32_t)(cn * 32), rb);
+              fetch_ops(n0 + cn * 32);
+            } else {
+              release();
+            }
+            process(ra, c);
+            if (!more) break;
+            c = cn;
+            stage_ops();
+            residual_load(c);
+            tmem_ld_wait_regs(rb);
+            cn = c + kParts;
+            more = ok && cn < nvalid;
+            if (more) {
+              tmem_ld_32x32b_x32(t_row + (uint32_t)(cn * 32), ra);
+              fetch_ops(n0 + cn * 32);
+            } else {
+              release();
+            }
+            process(rb, c);
+            if (!more) break;
+            c = cn;
+          }
+        }
+      } else {
+        // one register buffer (16 epilogue warps: the other warps hide the
+        // TMEM load latency)
+        uint32_t ra[32];
+        for (; ok && c < nvalid; c += kParts) {
+          stage_ops();
+          residual_load(c);
+          tmem_ld_32x32b_x32(t_row + (uint32_t)(c * 32), ra);
+          tmem_ld_wait_regs(ra);
+          const bool more = c + kParts < nvalid;
+          if (more) fetch_ops(n0 + (c + kParts) * 32);
+          else release();
+          process(ra, c);
+        }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[acc]);
+      if (!released) release();
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
     }
     if (tma_store && lane == 0) bulk_wait0();
     if (track) {
       // CTA-wide (min, max) of everything this CTA wrote: one partial per CTA
-      float2* red = reinterpret_cast<float2*>(tmem_slot + 2);  // 8-byte aligned slot area
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) {
         run_mn = fminf(run_mn, __shfl_xor_sync(0xffffffffu, run_mn, o));
         run_mx = fmaxf(run_mx, __shfl_xor_sync(0xffffffffu, run_mx, o));
       }
       if (lane == 0) red[e] = make_float2(run_mn, run_mx);
-      epi_sync();
+      epi_sync<EW>();
       if (e == 0 && lane == 0) {
         float mn = 0.0f, mx = 0.0f;
-        for (int i = 0; i < kEpiWarps; ++i) {
+        for (int i = 0; i < EW; ++i) {
           mn = fminf(mn, red[i].x);
           mx = fmaxf(mx, red[i].y);
         }
@@ -759,10 +863,10 @@ static int make_out_tmap(CUtensorMap* map, void* base, size_t M, size_t N, bool 
 
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
-template <int BN, int EPI, bool DEEP>
+template <int BN, int EPI, bool DEEP, int EW>
 static int launch_tc(cudaStream_t s, const void* a, bool a_signed, const void* bt,
                      bool b_signed, const GemmArgs& args) {
-  using C = Cfg<BN, DEEP>;
+  using C = Cfg<BN, DEEP, EW>;
   CUtensorMap ta, tb, tout;
   int rc = make_tmap(&ta, a, (size_t)args.M, (size_t)args.K, kBM);
   if (rc) return rc;
@@ -786,20 +890,33 @@ static int launch_tc(cudaStream_t s, const void* a, bool a_signed, const void* b
   const int vec_cols = (args.N % 4 == 0) && aligned16(args.colsum) &&
                        (args.w_scale == nullptr || !args.w_scale_per_col || aligned16(args.w_scale)) &&
                        (args.bias == nullptr || aligned16(args.bias));
-  auto kern = args.b_zp ? (args.bias ? qgemm_tcgen05_kernel<BN, EPI, true, true, DEEP>
-                                      : qgemm_tcgen05_kernel<BN, EPI, true, false, DEEP>)
-                        : (args.bias ? qgemm_tcgen05_kernel<BN, EPI, false, true, DEEP>
-                                     : qgemm_tcgen05_kernel<BN, EPI, false, false, DEEP>);
+  auto kern = args.b_zp ? (args.bias ? qgemm_tcgen05_kernel<BN, EPI, true, true, DEEP, EW>
+                                      : qgemm_tcgen05_kernel<BN, EPI, true, false, DEEP, EW>)
+                        : (args.bias ? qgemm_tcgen05_kernel<BN, EPI, false, true, DEEP, EW>
+                                     : qgemm_tcgen05_kernel<BN, EPI, false, false, DEEP, EW>);
   ICX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 C::kSmemBytes));
   const int ntiles = ((args.M + kBM - 1) / kBM) * ((args.N + BN - 1) / BN);
   int grid = sm_count();
   if (ntiles < grid) grid = ntiles;
   const uint32_t idesc = idesc_i8(kBM, BN, a_signed, b_signed);
-  launch_pdl(kern, dim3(grid), dim3(kThreads), C::kSmemBytes, s, ta, tb, tout, tres, args, idesc, tma_store, vec_cols,
+  launch_pdl(kern, dim3(grid), dim3(gemm_threads<EW>()), C::kSmemBytes, s, ta, tb, tout, tres, args, idesc, tma_store, vec_cols,
                                              tma_res);
   ICX_LAUNCH_CHECK();
   return ICX_OK;
+}
+
+// Epilogue warps of the shallow (K < 1536) f32 GEMMs: 16 for the GELU
+// variant, 8 for the others; ICX_GEMM_EPI_WARPS=8|16 overrides both (read
+// once per process, for measurement).
+static int epilogue_warps(bool gelu) {
+  static int forced = [] {
+    const char* v = getenv("ICX_GEMM_EPI_WARPS");
+    const int n = v ? atoi(v) : 0;
+    return n == 8 || n == 16 ? n : 0;
+  }();
+  if (forced) return forced;
+  return gelu ? 16 : 8;
 }
 
 // Which kernel runs a GEMM and with how many CTAs.
@@ -848,15 +965,21 @@ static int launch_gemm(cudaStream_t s, const void* a, bool a_signed,
   if (args.M == 0 || args.N == 0) return ICX_OK;
   const GemmPlan p = plan_gemm(args, a, bt);
   const bool deep = args.K >= 1536;
+  // 16 epilogue warps (more TMEM loads and math in flight) for the shallow
+  // GELU GEMM, whose epilogue is the bottleneck; 8 otherwise
+  const bool ew16 = !deep && EPI != kEpiS32 && epilogue_warps(EPI == kEpiGelu) == 16;
   if (p.bn == 256)
-    return deep ? launch_tc<256, EPI, true>(s, a, a_signed, bt, b_signed, args)
-                : launch_tc<256, EPI, false>(s, a, a_signed, bt, b_signed, args);
+    return deep   ? launch_tc<256, EPI, true, 8>(s, a, a_signed, bt, b_signed, args)
+           : ew16 ? launch_tc<256, EPI, false, (EPI == kEpiS32 ? 8 : 16)>(s, a, a_signed, bt, b_signed, args)
+                  : launch_tc<256, EPI, false, 8>(s, a, a_signed, bt, b_signed, args);
   if (p.bn == 192)
-    return deep ? launch_tc<192, EPI, true>(s, a, a_signed, bt, b_signed, args)
-                : launch_tc<192, EPI, false>(s, a, a_signed, bt, b_signed, args);
+    return deep   ? launch_tc<192, EPI, true, 8>(s, a, a_signed, bt, b_signed, args)
+           : ew16 ? launch_tc<192, EPI, false, (EPI == kEpiS32 ? 8 : 16)>(s, a, a_signed, bt, b_signed, args)
+                  : launch_tc<192, EPI, false, 8>(s, a, a_signed, bt, b_signed, args);
   if (p.bn == 128)
-    return deep ? launch_tc<128, EPI, true>(s, a, a_signed, bt, b_signed, args)
-                : launch_tc<128, EPI, false>(s, a, a_signed, bt, b_signed, args);
+    return deep   ? launch_tc<128, EPI, true, 8>(s, a, a_signed, bt, b_signed, args)
+           : ew16 ? launch_tc<128, EPI, false, (EPI == kEpiS32 ? 8 : 16)>(s, a, a_signed, bt, b_signed, args)
+                  : launch_tc<128, EPI, false, 8>(s, a, a_signed, bt, b_signed, args);
   const size_t total = (size_t)args.M * args.N;
   const int threads = 256;
   const size_t blocks = (total + threads - 1) / threads;

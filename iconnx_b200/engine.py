@@ -244,6 +244,37 @@ class GpuGraphExecutor:
     def kernel_launches(self) -> int:
         return int(self._L.icx_engine_kernel_launches(self._h))
 
+    # ------------------------------------------------ per-step debug access
+    def steps(self) -> list[tuple[str, str, str, dict]]:
+        """The compiled plan's steps as (op, node, output, info) where info
+        maps the names of the values the step reads and writes (see
+        icx_engine_step_info).  Empty before the first run."""
+        out = []
+        for i in range(int(self._L.icx_engine_step_count(self._h))):
+            raw = self._L.icx_engine_step_info(self._h, i)
+            if raw is None:
+                raise IcxError(-1, self._L.icx_last_error().decode())
+            op, node, o, info = raw.decode().split("\t", 3)
+            kv = dict(item.split("=", 1) for item in info.split(";") if "=" in item)
+            out.append((op, node, o, kv))
+        return out
+
+    def run_step(self, i: int) -> None:
+        """Runs plan step ``i`` alone and waits for it (call in plan order,
+        after a run, to re-execute the plan stage by stage)."""
+        check(self._L.icx_engine_run_step(self._h, int(i)))
+
+    def value(self, name: str) -> np.ndarray:
+        """Current contents of any value the compiled plan materialises."""
+        dt, rk = ctypes.c_int(), ctypes.c_int()
+        dims = (ctypes.c_int64 * 6)()
+        check(self._L.icx_engine_value_info(self._h, name.encode(), ctypes.byref(dt),
+                                            ctypes.byref(rk), dims))
+        out = np.empty(tuple(dims[i] for i in range(rk.value)), dtype=_ICX2NP[dt.value])
+        check(self._L.icx_engine_value_copy(self._h, name.encode(),
+                                            out.ctypes.data_as(ctypes.c_void_p), out.nbytes))
+        return out
+
     def set_cuda_graphs(self, enabled: bool) -> None:
         check(self._L.icx_engine_set_cuda_graphs(self._h, int(enabled)))
 

@@ -300,6 +300,32 @@ ICX_API void* icx_engine_stream(icx_engine* e);
 /* Kernel launches per run of the compiled plan. */
 ICX_API int icx_engine_kernel_launches(icx_engine* e);
 
+/* Per-step debug interface: stage-by-stage inspection of the compiled, fused
+ * plan without turning fusion off (requesting an intermediate as an output
+ * would keep it materialised and change the plan).  Replaces the reference's
+ * intermediate-value access in its debug / validation runs
+ * (src/cuda/inference/mod.rs:88-164 ProfileData, src/cuda/executor/
+ * variants.rs:415 run_with_profiling), which record per-node results.
+ *   step_count: steps of the compiled plan (0 before the first run).
+ *   step_info:  "op\tnode\toutput\tkey=value;..." naming the values step i
+ *               reads and writes (fused Linears: q, s, z, w, ws, bz, bias,
+ *               residual, gelu, out; merged Linears list their parts'
+ *               initializers '|'-separated; other steps: in=..., outs=...).
+ *               NULL if i is out of range.  Valid until the next call.
+ *   run_step:   runs step i alone, eagerly, and waits for it.  After a run,
+ *               calling it for i = 0, 1, ... in order re-executes the plan
+ *               step by step; the values a step reads are live in the arena
+ *               just before it runs and the values it writes just after.
+ *   value_info / value_copy: shape and current contents of any value the
+ *               plan materialises (ICX_ERR_NOT_FOUND for values that live
+ *               inside a fused kernel). */
+ICX_API int icx_engine_step_count(icx_engine* e);
+ICX_API const char* icx_engine_step_info(icx_engine* e, int i);
+ICX_API int icx_engine_run_step(icx_engine* e, int i);
+ICX_API int icx_engine_value_info(icx_engine* e, const char* name, int* dtype, int* rank,
+                                  int64_t* dims /* [6] */);
+ICX_API int icx_engine_value_copy(icx_engine* e, const char* name, void* host, size_t bytes);
+
 #ifdef __cplusplus
 }
 #endif

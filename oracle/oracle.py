@@ -167,3 +167,35 @@ def quant_linear(x: np.ndarray, w: np.ndarray, w_scale, bias: np.ndarray, b_zp=N
 
 def max_threads() -> int:
     return int(lib().oracle_max_threads())
+
+
+def quant_linear_from_q(q: np.ndarray, a_scale, a_zp, w: np.ndarray, w_scale, bias=None,
+                        b_zp=None, gelu: bool = False, residual: np.ndarray | None = None,
+                        threads: int = 1) -> np.ndarray:
+    """The Linear chain after DynamicQuantizeLinear, on its outputs:
+    MatMulInteger(q, w, a_zp, b_zp) (matmul_integer.rs:239-267) -> Cast
+    (cast.rs:46-48) -> Mul(., Mul(a_scale, w_scale)) (mul.rs:26-58) ->
+    [Add(bias) (add.rs:27-85)] [-> GELU subgraph (erf.rs:30-40)]
+    [-> Add(residual)], each op rounded on its own as the reference's CPU
+    GraphExecutor runs them one node at a time.  q u8 [M, K]; returns f32 [M, N]."""
+    q = np.ascontiguousarray(q, dtype=np.uint8)
+    M = q.shape[0]
+    N = w.shape[1]
+    acc = matmul_integer(q, np.ascontiguousarray(w), np.uint8(a_zp), b_zp, threads=threads)
+    c = cast_i32_f32(acc)
+    ws = np.ascontiguousarray(np.atleast_1d(np.asarray(w_scale, dtype=np.float32)))
+    s = np.empty(ws.size, dtype=np.float32)
+    L = lib()
+    L.oracle_mul_scalar_vec(ctypes.c_float(float(np.float32(a_scale))), _p(ws), ws.size, _p(s))
+    o = np.empty((M, N), dtype=np.float32)
+    L.oracle_mul_rows(_p(c), M, N, _p(s), s.size, _p(o))
+    if bias is not None:
+        b = np.ascontiguousarray(bias, dtype=np.float32)
+        o2 = np.empty_like(o)
+        L.oracle_add_bias(_p(o), M, N, _p(b), _p(o2))
+        o = o2
+    if gelu:
+        o = globals()["gelu"](o)
+    if residual is not None:
+        o = np.add(o, np.ascontiguousarray(residual, dtype=np.float32), dtype=np.float32)
+    return o
