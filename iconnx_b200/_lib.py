@@ -24,6 +24,7 @@ PROTOTYPES = {
     "icx_last_error": (ctypes.c_char_p, []),
     "icx_version": (ctypes.c_char_p, []),
     "icx_device_status": (_i, [_i, _vp]),
+    "icx_selftest_bounded_wait": (_i, [_vp, ctypes.c_uint64]),
     "icx_dql_workspace_bytes": (_sz, [_sz]),
     "icx_dql_f32_u8": (_i, [_vp, _vp, _sz, _vp, _vp, _vp, _vp, _sz, _vp, _sz]),
     "icx_prepare_b": (_i, [_vp, _vp, _i, _sz, _sz, _vp, _vp]),

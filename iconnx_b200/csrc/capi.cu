@@ -19,7 +19,30 @@ void set_error(const char* fmt, ...) {
 
 void clear_error() { t_last_error.clear(); }
 
+// One warp waits on an mbarrier that nothing arrives on: the bounded wait
+// gives up after limit_ns, records ICX_DEVICE_TIMEOUT_SELFTEST and the kernel
+// returns normally.
+__global__ void bounded_wait_selftest_kernel(uint64_t limit_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) mbar_wait(&bar, 0, ICX_DEVICE_TIMEOUT_SELFTEST, limit_ns);
+  __syncwarp();
+}
+
 }  // namespace icx
+
+extern "C" int icx_selftest_bounded_wait(void* stream, uint64_t limit_ns) {
+  ICX_REQUIRE(limit_ns > 0 && limit_ns <= 100000000ull,
+              "selftest_bounded_wait: limit %llu ns outside (0, 100 ms]",
+              (unsigned long long)limit_ns);
+  icx::bounded_wait_selftest_kernel<<<1, 32, 0, icx::as_stream(stream)>>>(limit_ns);
+  ICX_LAUNCH_CHECK();
+  return ICX_OK;
+}
 
 extern "C" const char* icx_last_error(void) {
   return icx::t_last_error.c_str();

@@ -128,15 +128,17 @@ __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, i
 }
 
 // Bounded wait for the phase with the given parity to complete.  Returns
-// false (and records `code`) when the limit is reached.
+// false (and records `code`) when the limit is reached.  Spins on try_wait
+// (which itself suspends the thread in hardware for a while before it
+// reports failure) and reads the clock only every 64 polls, so a phase that
+// completes is seen at once.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
-                                          int code) {
+                                          int code, uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   uint32_t n = 0;
   while (!mbar_try_wait(bar, parity)) {
-    if (++n > 64) __nanosleep(64);
-    if ((n & 255) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
+    if ((++n & 63) == 0 && globaltimer_ns() - t0 > limit_ns) {
       record_status(code);
       return false;
     }

@@ -432,11 +432,16 @@ extern "C" int icx_dql_quantize_f32_u8(void* stream, const float* d_x, size_t n,
 //
 // The array holds ICX_MAX_MINMAX_PARTIALS pairs (9472 bytes) and stays
 // resident on every GPU that loads this library until the process exits.
+// Each pair summarises at most 2^17 elements of x on this path, so the
+// largest input is ICX_DQL_NOALLOC_MAX_N = 1184 * 2^17 elements (592 MiB of
+// f32); larger inputs are rejected before any launch.
 // Nothing in it needs clearing between calls: every block of the min/max pass
 // overwrites its own slot before the quantise pass reads it.  All calls on a
 // device share the one array, so two calls whose kernels overlap on the GPU
 // (different streams, no ordering between them) race on it.
 static __device__ __align__(256) float2 g_dql_noalloc_scratch[ICX_MAX_MINMAX_PARTIALS];
+static_assert(ICX_DQL_NOALLOC_MAX_N == (unsigned long long)ICX_MAX_MINMAX_PARTIALS << 17,
+              "the no-alloc limit is 2^17 elements per scratch pair");
 
 namespace icx {
 namespace {
@@ -446,7 +451,11 @@ float2* g_noalloc_ptr[kNoallocMaxDevices] = {};
 
 // Device address of the scratch array on the current device.  The symbol's
 // name in host code is only a host-side handle; the real address comes from
-// cudaGetSymbolAddress, looked up once per device with that device current.
+// cudaGetSymbolAddress, looked up once per device with that device current
+// and cached for the life of the process.  The cache assumes the primary
+// context: after cudaDeviceReset (or with another context current on the
+// device) the module is loaded again at a new address, and the cached
+// pointer would be stale.
 int noalloc_scratch(float2** out) {
   int dev = 0;
   ICX_CUDA(cudaGetDevice(&dev));
@@ -473,10 +482,8 @@ extern "C" int icx_dql_f32_u8_noalloc(void* stream, const float* d_x, size_t n,
   ICX_REQUIRE(n == 0 || (d_x && d_y), "DynamicQuantizeLinear: null x or y");
   ICX_REQUIRE(d_rowsum == nullptr || (row_len > 0 && n % row_len == 0),
               "DynamicQuantizeLinear: row_len %zu must divide n %zu", row_len, n);
+  // at most ICX_MAX_MINMAX_PARTIALS blocks, each writing one scratch pair
   const int blocks = minmax_blocks(n);
-  ICX_REQUIRE(blocks <= ICX_MAX_MINMAX_PARTIALS,
-              "DynamicQuantizeLinear (no-alloc): %d partials exceed the scratch of %d", blocks,
-              ICX_MAX_MINMAX_PARTIALS);
   float2* scratch = nullptr;
   int rc = noalloc_scratch(&scratch);
   if (rc) return rc;

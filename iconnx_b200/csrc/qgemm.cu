@@ -108,10 +108,12 @@ constexpr int gemm_threads() { return 64 + 32 * EW; }
 // them with broadcast loads, and for double-buffered output staging.
 template <int BN, bool DEEP, int EW>
 struct Cfg {
-  // (16 epilogue warps take one stage more for their staging boxes)
-  static constexpr int kStages = BN == 256 ? (DEEP ? 4 : 3)
-                                 : BN == 192 ? (EW == 16 ? 3 : 4)
-                                             : (DEEP ? 6 : (EW == 16 ? 4 : 5));
+  // DEEP GEMMs keep a deeper ring and one output staging box per warp; 16
+  // epilogue warps take one stage fewer for their staging boxes.
+  static constexpr int kStages = DEEP ? (BN == 256 ? 4 : BN == 192 ? 4 : 5)
+                                      : BN == 256 ? 3
+                                      : BN == 192 ? (EW == 16 ? 3 : 4)
+                                                  : (EW == 16 ? 4 : 5);
   static constexpr int kABytes = kBM * kBK;
   static constexpr int kBBytes = BN * kBK;
   static constexpr int kStageBytes = kABytes + kBBytes;
@@ -119,12 +121,15 @@ struct Cfg {
   static constexpr int kTmemCols = BN == 192 ? 512 : 2 * BN;
   static constexpr int kOutOffset = kStages * kStageBytes;
   // per-warp column operands of one 32-column chunk: colsum, scale, bias, b_zp
-  static constexpr int kOpWarpBytes = DEEP ? 0 : 4 * 32 * 4;
+  // (all but the 256-wide DEEP tile, whose 4-stage ring leaves no room: that
+  // one reads the operands from global memory through L1)
+  static constexpr bool kStageOps = !(DEEP && BN == 256);
+  static constexpr int kOpWarpBytes = kStageOps ? 4 * 32 * 4 : 0;
   static constexpr int kBarBytes = 1024;
   static constexpr int kFixed = kOutOffset + EW * kOpWarpBytes + kBarBytes + 1024 /*align slack*/;
   // two output staging boxes per warp when they fit (a warp fills one while
   // the TMA store of the other drains)
-  static constexpr int kOutBufs = kFixed + 2 * EW * kStageOutBytes <= 227 * 1024 ? 2 : 1;
+  static constexpr int kOutBufs = DEEP ? 1 : kFixed + 2 * EW * kStageOutBytes <= 227 * 1024 ? 2 : 1;
   static constexpr int kOpOffset = kOutOffset + kOutBufs * EW * kStageOutBytes;
   static constexpr int kBarOffset = kOpOffset + EW * kOpWarpBytes;
   static constexpr int kSmemBytes = kBarOffset + kBarBytes + 1024;
@@ -427,7 +432,8 @@ __global__ void __launch_bounds__(gemm_threads<EW>(), 1)
     const bool sc_per_col = args.w_scale_per_col != 0;
     const bool bz_per_col = args.b_zp_per_col != 0;
     const int32_t bz_scalar = HAS_BZ ? ld_zp(args.b_zp, args.b_zp_signed, 0) : 0;
-    const bool vec = vec_cols != 0;
+    const bool vec = (vec_cols & 1) != 0;
+    const bool bz_vec = (vec_cols & 2) != 0;  // per-column b_zp readable as 4-byte words
     // this warp's operand slice: colsum, scale, bias, b_zp of one chunk
     int32_t* op_cs = reinterpret_cast<int32_t*>(smem + C::kOpOffset + e * C::kOpWarpBytes);
     float* op_sc = reinterpret_cast<float*>(op_cs + 32);
@@ -445,7 +451,7 @@ __global__ void __launch_bounds__(gemm_threads<EW>(), 1)
     int32_t p_cs = 0, p_bz = 0;
     float p_sc = 0.0f, p_bi = 0.0f;
     auto fetch_ops = [&](int nb) {
-      if (DEEP) return;
+      if (!C::kStageOps) return;
       const int n = nb + lane;
       p_cs = 0;
       p_sc = sc_scalar;
@@ -459,7 +465,7 @@ __global__ void __launch_bounds__(gemm_threads<EW>(), 1)
       }
     };
     auto stage_ops = [&]() {
-      if (DEEP) return;
+      if (!C::kStageOps) return;
       __syncwarp();  // every lane is done with the previous chunk's slice
       op_cs[lane] = p_cs;
       op_sc[lane] = (EPI != kEpiS32 && sc_per_col) ? __fmul_rn(a_scale, p_sc) : p_sc;
@@ -477,7 +483,7 @@ __global__ void __launch_bounds__(gemm_threads<EW>(), 1)
       if (HAS_BZ) kza_rs = (uint32_t)K * za - ((m < M) ? (uint32_t)args.rowsum[m] : 0u);
       // chunks of this tile that hold columns < N
       const int nvalid = min(kChunks, (N - n0 + 31) / 32);
-      if (DEEP) {
+      if (!C::kStageOps) {
         // per-column operands come from global memory: pull them into L1
         const int et = threadIdx.x - 64;
         if (et < BN * 4 / 128) {
@@ -509,7 +515,7 @@ __global__ void __launch_bounds__(gemm_threads<EW>(), 1)
         const int nb = n0 + cc * 32;
         uint8_t* stage_out = sOut + (obuf * EW + e) * kStageOutBytes;
         const bool res_tma = EPI == kEpiF32 && tma_res && mrow0 < M;
-        const bool fast = DEEP ? (vec && (nb + 32 <= N) && !(HAS_BZ && bz_per_col)) : true;
+        const bool fast = C::kStageOps || (vec && (nb + 32 <= N) && (!(HAS_BZ && bz_per_col) || bz_vec));
         if (fast) {
 #pragma unroll
           for (int q = 0; q < 8; ++q) {
@@ -517,7 +523,7 @@ __global__ void __launch_bounds__(gemm_threads<EW>(), 1)
             float4 sc = make_float4(sc_scalar, sc_scalar, sc_scalar, sc_scalar);
             float4 bi = make_float4(0.f, 0.f, 0.f, 0.f);
             int4 bz = make_int4(bz_scalar, bz_scalar, bz_scalar, bz_scalar);
-            if (DEEP) {
+            if (!C::kStageOps) {
               cs = __ldg(reinterpret_cast<const int4*>(args.colsum + nb) + q);
               if (EPI != kEpiS32 && sc_per_col) {
                 const float4 w = __ldg(reinterpret_cast<const float4*>(args.w_scale + nb) + q);
@@ -525,6 +531,17 @@ __global__ void __launch_bounds__(gemm_threads<EW>(), 1)
                                  __fmul_rn(a_scale, w.z), __fmul_rn(a_scale, w.w));
               }
               if (EPI != kEpiS32 && HAS_BIAS) bi = __ldg(reinterpret_cast<const float4*>(args.bias + nb) + q);
+              if (HAS_BZ && bz_per_col) {
+                // four 8-bit zero points in one 32-bit load
+                const uint32_t w = __ldg(reinterpret_cast<const uint32_t*>(
+                                             static_cast<const uint8_t*>(args.b_zp) + nb) + q);
+                if (args.b_zp_signed)
+                  bz = make_int4((int8_t)(w & 0xff), (int8_t)((w >> 8) & 0xff), (int8_t)((w >> 16) & 0xff),
+                                 (int8_t)(w >> 24));
+                else
+                  bz = make_int4((int)(w & 0xff), (int)((w >> 8) & 0xff), (int)((w >> 16) & 0xff),
+                                 (int)(w >> 24));
+              }
             } else {
               cs = reinterpret_cast<const int4*>(op_cs)[q];
               if (EPI != kEpiS32 && sc_per_col) sc = reinterpret_cast<const float4*>(op_sc)[q];
@@ -630,7 +647,7 @@ __global__ void __launch_bounds__(gemm_threads<EW>(), 1)
           if (mrow0 < M) {
             // this box's previous store (kOutBufs chunks ago) must have been
             // read out of shared memory (the residual path waited already)
-            if (lane == 0 && !res_tma) bulk_wait_read<C::kOutBufs - 1>();
+            if (lane == 0 && !res_tma) bulk_wait_read<(C::kOutBufs > 1 ? 1 : 0)>();
             __syncwarp();
             uint8_t* row = stage_out + lane * 128;
 #pragma unroll
@@ -647,15 +664,21 @@ __global__ void __launch_bounds__(gemm_threads<EW>(), 1)
           }
         } else if (m < M) {
           uint32_t* orow = static_cast<uint32_t*>(args.out) + (size_t)m * N + nb;
+          if (vec && nb + 32 <= N && (reinterpret_cast<uintptr_t>(args.out) & 15) == 0) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (nb + j < N) orow[j] = r[j];
+            for (int q = 0; q < 8; ++q)
+              reinterpret_cast<uint4*>(orow)[q] = make_uint4(r[4 * q], r[4 * q + 1], r[4 * q + 2], r[4 * q + 3]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (nb + j < N) orow[j] = r[j];
+          }
         }
       };
       // residual box of chunk cc -> the staging box it will be stored from
       auto residual_load = [&](int cc) {
         if (EPI == kEpiF32 && tma_res && mrow0 < M && lane == 0) {
-          bulk_wait_read<C::kOutBufs - 1>();
+          bulk_wait_read<(C::kOutBufs > 1 ? 1 : 0)>();
           uint8_t* stage_out = sOut + (obuf * EW + e) * kStageOutBytes;
           mbar_arrive_expect_tx(&rbar[e], kStageOutBytes);
           tma_load_2d(stage_out, &tmRes, &rbar[e], n0 + cc * 32, mrow0);
@@ -873,7 +896,7 @@ static int launch_tc(cudaStream_t s, const void* a, bool a_signed, const void* b
   rc = make_tmap(&tb, bt, (size_t)args.N, (size_t)args.K, BN);
   if (rc) return rc;
   // TMA stores need a 16-byte aligned base and a row pitch multiple of 16 B
-  const int tma_store = (args.N % 4 == 0) && aligned16(args.out);
+  const int tma_store = C::kOutBufs > 0 && (args.N % 4 == 0) && aligned16(args.out);
   if (tma_store) {
     rc = make_out_tmap(&tout, args.out, (size_t)args.M, (size_t)args.N, EPI != kEpiS32);
     if (rc) return rc;
@@ -887,9 +910,14 @@ static int launch_tc(cudaStream_t s, const void* a, bool a_signed, const void* b
     rc = make_out_tmap(&tres, const_cast<float*>(args.residual), (size_t)args.M, (size_t)args.N, true);
     if (rc) return rc;
   }
-  const int vec_cols = (args.N % 4 == 0) && aligned16(args.colsum) &&
-                       (args.w_scale == nullptr || !args.w_scale_per_col || aligned16(args.w_scale)) &&
-                       (args.bias == nullptr || aligned16(args.bias));
+  // bit 0: 16-byte vector loads of the column operands; bit 1: per-column
+  // zero points readable as aligned 4-byte words
+  const int vec_cols = ((args.N % 4 == 0) && aligned16(args.colsum) &&
+                        (args.w_scale == nullptr || !args.w_scale_per_col || aligned16(args.w_scale)) &&
+                        (args.bias == nullptr || aligned16(args.bias)))
+                           ? 1 | ((args.b_zp && args.b_zp_per_col &&
+                                   (reinterpret_cast<uintptr_t>(args.b_zp) & 3) == 0) ? 2 : 0)
+                           : 0;
   auto kern = args.b_zp ? (args.bias ? qgemm_tcgen05_kernel<BN, EPI, true, true, DEEP, EW>
                                       : qgemm_tcgen05_kernel<BN, EPI, true, false, DEEP, EW>)
                         : (args.bias ? qgemm_tcgen05_kernel<BN, EPI, false, true, DEEP, EW>

@@ -50,6 +50,7 @@ extern "C" {
 #define ICX_DEVICE_TIMEOUT_PRODUCER 0x101
 #define ICX_DEVICE_TIMEOUT_MMA 0x102
 #define ICX_DEVICE_TIMEOUT_EPILOGUE 0x103
+#define ICX_DEVICE_TIMEOUT_SELFTEST 0x1ff
 
 /* Upper bound on the (min, max) partial pairs a producer writes for a
  * following DynamicQuantizeLinear (icx_quant_linear d_minmax, and the
@@ -73,6 +74,14 @@ ICX_API const char* icx_version(void);
 /* Reads and clears the device-side status word of `device` (0 = no kernel
  * gave up on a bounded wait since the last call). */
 ICX_API int icx_device_status(int device, int* status_out);
+
+/* Self-test of the kernels' failure handling (no reference counterpart; the
+ * reference's kernels have no bounded waits): enqueues one tiny kernel whose
+ * bounded mbarrier wait can never complete, with a limit of limit_ns
+ * (0 < limit_ns <= 100 ms) instead of the kernels' 2 s.  The wait gives up,
+ * records ICX_DEVICE_TIMEOUT_SELFTEST for icx_device_status and the kernel
+ * returns, leaving the context usable; no fault, trap or hang. */
+ICX_API int icx_selftest_bounded_wait(void* stream, uint64_t limit_ns);
 
 /* ======================================================================== *
  * DynamicQuantizeLinear
@@ -101,13 +110,16 @@ ICX_API int icx_dql_f32_u8(void* stream, const float* d_x, size_t n, uint8_t* d_
  * results as icx_dql_f32_u8, but the scratch lives in a 9472-byte array
  * compiled into this library (resident on each GPU that loads it until the
  * process exits) instead of a caller workspace.  Calls no allocator.
- * Limit: n <= ICX_DQL_NOALLOC_MAX_N, larger n is rejected with
- * ICX_ERR_INVALID.  The first call on a device looks up the array's device
- * address (cudaGetSymbolAddress); make that first call before any stream
- * capture.  All calls on a device share the array: calls whose kernels may
- * overlap on the GPU (e.g. unordered streams) race and must be serialised by
- * the caller. */
-#define ICX_DQL_NOALLOC_MAX_N (1ull << 32)
+ * Limit: each of the array's ICX_MAX_MINMAX_PARTIALS (min, max) pairs
+ * summarises at most 2^17 elements, so n <= ICX_DQL_NOALLOC_MAX_N
+ * (155,189,248 elements); larger n is rejected with ICX_ERR_INVALID before
+ * any launch.  The first call on a device looks up the array's device
+ * address (cudaGetSymbolAddress) and caches it for the process: make that
+ * first call before any stream capture, and do not use this entry point
+ * after cudaDeviceReset.  All calls on a device share the array: calls whose
+ * kernels may overlap on the GPU (e.g. unordered streams) race and must be
+ * serialised by the caller. */
+#define ICX_DQL_NOALLOC_MAX_N (1184ull << 17)
 ICX_API int icx_dql_f32_u8_noalloc(void* stream, const float* d_x, size_t n,
                                    uint8_t* d_y, float* d_scale, uint8_t* d_zp,
                                    int32_t* d_rowsum, size_t row_len);

@@ -4,35 +4,40 @@ icx_dql_f32_u8_noalloc serves callers that may not allocate device memory
 while they run (a memory budget fixed at start-up, an allocator that cannot
 be re-entered from the calling thread, a host that bans cudaMalloc because it
 can synchronise the device).  It keeps its scratch in an array compiled into
-the library.  These tests call it through the C ABI and check that it gives
-exactly what the workspace-taking entry point gives, on two calls in a row
-(the second call reuses the array the first one left behind).
+the library.  These tests call it through the C ABI and check it, call after
+call on the same array, against both the workspace-taking entry point and the
+oracle restatement of the reference operator
+(src/operators/dynamic_quantize_linear.rs:32-112): bit-exact u8 output,
+scale, zero point and row sums.
 
 This file is named so that pytest collects it last.
 """
-import ctypes
-
 import numpy as np
 import pytest
 
 from iconnx_b200 import _lib, synth
 
+NOALLOC_MAX_N = 1184 << 17   # ICX_DQL_NOALLOC_MAX_N
+
 
 def test_noalloc_rejects_oversized_input_before_any_launch():
     L = _lib.load()
-    too_big = (1 << 32) + 1
-    rc = L.icx_dql_f32_u8_noalloc(None, None, too_big, None, None, None, None, 0)
+    rc = L.icx_dql_f32_u8_noalloc(None, None, NOALLOC_MAX_N + 1, None, None, None, None, 0)
     assert rc == -1  # ICX_ERR_INVALID
     assert b"exceeds the maximum" in L.icx_last_error()
 
 
 @pytest.mark.gpu
-def test_noalloc_matches_workspace_entry_point_twice():
+def test_noalloc_matches_workspace_entry_point_and_oracle_call_after_call():
     import torch
+    from oracle import oracle
     L = _lib.load()
     dev = "cuda:0"
-    cases = [(synth.normal((4096, 768), 1.0, 31), 768),     # large: many partials
-             (synth.outlier_mix((37, 20), 32), 20)]          # small: one partial, odd rows
+    # large (1184 scratch pairs written), then mid-size (fewer pairs than the
+    # previous call left in the array, different values), then small (one pair)
+    cases = [(synth.normal((4096, 768), 1.0, 31), 768),
+             (synth.outlier_mix((300, 768), 33) * np.float32(3.0), 768),
+             (synth.outlier_mix((37, 20), 32), 20)]
     stream = torch.cuda.current_stream(dev).cuda_stream
     for x_np, row_len in cases:
         x = torch.from_numpy(x_np).to(dev).reshape(-1)
@@ -55,3 +60,8 @@ def test_noalloc_matches_workspace_entry_point_twice():
         torch.cuda.synchronize()
         for r, g in zip(ref, got):
             np.testing.assert_array_equal(g.cpu().numpy(), r.cpu().numpy())
+        oy, os_, oz = oracle.dynamic_quantize_linear(x_np)
+        np.testing.assert_array_equal(got[0].cpu().numpy(), oy.reshape(-1))
+        assert got[1].item() == os_ and got[2].item() == oz
+        np.testing.assert_array_equal(got[3].cpu().numpy(),
+                                      oracle.rowsum_u8(oy.reshape(-1, row_len)))
