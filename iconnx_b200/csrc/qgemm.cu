@@ -106,30 +106,37 @@ constexpr int gemm_threads() { return 64 + 32 * EW; }
 // one stage fewer pays for staging each chunk's column operands in a per-warp
 // shared-memory slice, where the epilogue (the bottleneck at small K) reads
 // them with broadcast loads, and for double-buffered output staging.
-template <int BN, bool DEEP, int EW>
+template <int BN, bool DEEP, int EW, int CG = 1>
 struct Cfg {
-  // DEEP GEMMs keep a deeper ring and one output staging box per warp; 16
-  // epilogue warps take one stage fewer for their staging boxes.
-  static constexpr int kStages = DEEP ? (BN == 256 ? 4 : BN == 192 ? 4 : 5)
-                                      : BN == 256 ? 3
-                                      : BN == 192 ? (EW == 16 ? 3 : 4)
-                                                  : (EW == 16 ? 4 : 5);
   static constexpr int kABytes = kBM * kBK;
-  static constexpr int kBBytes = BN * kBK;
+  // CG == 2 (a CTA pair computing a 256 x BN tile with cta_group::2): each
+  // CTA holds its 128 rows of A and BN / 2 rows of B
+  static constexpr int kBBytes = (BN / CG) * kBK;
   static constexpr int kStageBytes = kABytes + kBBytes;
+  // per-warp column operands of one 32-column chunk: colsum, scale, bias, b_zp
+  // (all but the 256-wide DEEP single-CTA tile, whose 4-stage ring leaves no
+  // room: that one reads the operands from global memory through L1)
+  static constexpr bool kStageOps = !(DEEP && BN == 256 && CG == 1);
+  static constexpr int kOpWarpBytes = kStageOps ? 4 * 32 * 4 : 0;
+  static constexpr int kBarBytes = 1024;
+  // Single CTA: DEEP GEMMs keep a deeper ring and one output staging box per
+  // warp; 16 epilogue warps take one stage fewer for their staging boxes.
+  // CTA pairs: as many stages as fit beside one staging box per warp.
+  static constexpr int kPairStages =
+      (227 * 1024 - EW * kStageOutBytes - EW * kOpWarpBytes - kBarBytes - 1024) / kStageBytes;
+  static constexpr int kStages = CG == 2 ? (kPairStages > 8 ? 8 : kPairStages)
+                                 : DEEP ? (BN == 256 ? 4 : BN == 192 ? 4 : 5)
+                                 : BN == 256 ? 3
+                                 : BN == 192 ? (EW == 16 ? 3 : 4)
+                                             : (EW == 16 ? 4 : 5);
   // two accumulators of BN columns; the allocation is a power of two
   static constexpr int kTmemCols = BN == 192 ? 512 : 2 * BN;
   static constexpr int kOutOffset = kStages * kStageBytes;
-  // per-warp column operands of one 32-column chunk: colsum, scale, bias, b_zp
-  // (all but the 256-wide DEEP tile, whose 4-stage ring leaves no room: that
-  // one reads the operands from global memory through L1)
-  static constexpr bool kStageOps = !(DEEP && BN == 256);
-  static constexpr int kOpWarpBytes = kStageOps ? 4 * 32 * 4 : 0;
-  static constexpr int kBarBytes = 1024;
   static constexpr int kFixed = kOutOffset + EW * kOpWarpBytes + kBarBytes + 1024 /*align slack*/;
   // two output staging boxes per warp when they fit (a warp fills one while
   // the TMA store of the other drains)
-  static constexpr int kOutBufs = DEEP ? 1 : kFixed + 2 * EW * kStageOutBytes <= 227 * 1024 ? 2 : 1;
+  static constexpr int kOutBufs =
+      (DEEP || CG == 2) ? 1 : kFixed + 2 * EW * kStageOutBytes <= 227 * 1024 ? 2 : 1;
   static constexpr int kOpOffset = kOutOffset + kOutBufs * EW * kStageOutBytes;
   static constexpr int kBarOffset = kOpOffset + EW * kOpWarpBytes;
   static constexpr int kSmemBytes = kBarOffset + kBarBytes + 1024;
@@ -138,6 +145,8 @@ struct Cfg {
   static_assert((2 * kStages + 4) * 8 <= 192, "barrier area");
   static_assert(EW * 8 <= 256, "per-warp slots");
   static_assert(EW % 4 == 0, "whole warps per TMEM lane quadrant");
+  static_assert(kStages >= 2, "at least two stages");
+  static_assert(CG == 1 || CG == 2, "one CTA or a CTA pair");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory");
 };
 
@@ -281,7 +290,7 @@ __device__ __forceinline__ float4 ld4f(const float* p, int n, int N, bool vec) {
                      n + 3 < N ? p[n + 3] : 0.f);
 }
 
-template <int BN, int EPI, bool HAS_BZ, bool HAS_BIAS, bool DEEP, int EW>
+template <int BN, int EPI, bool HAS_BZ, bool HAS_BIAS, bool DEEP, int EW, int CG>
 __global__ void __launch_bounds__(gemm_threads<EW>(), 1)
     qgemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA,
                          const __grid_constant__ CUtensorMap tmB,
@@ -289,7 +298,7 @@ __global__ void __launch_bounds__(gemm_threads<EW>(), 1)
                          const __grid_constant__ CUtensorMap tmRes,
                          const GemmArgs args, uint32_t idesc, int tma_store, int vec_cols,
                          int tma_res) {
-  using C = Cfg<BN, DEEP, EW>;
+  using C = Cfg<BN, DEEP, EW, CG>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -310,9 +319,13 @@ __global__ void __launch_bounds__(gemm_threads<EW>(), 1)
   const int lane = threadIdx.x & 31;
   const int M = args.M, N = args.N, K = args.K;
   const int num_n = (N + BN - 1) / BN;
-  const int num_m = (M + kBM - 1) / kBM;
+  const int num_m = (M + kBM * CG - 1) / (kBM * CG);   // tiles are kBM * CG rows
   const int ntiles = num_m * num_n;
   const int nk = (K + kBK - 1) / kBK;
+  // CTA pairs: rank within the pair (0 = leader), the pair's index and count
+  const uint32_t rank = CG == 2 ? cluster_ctarank() : 0u;
+  const int tile0 = CG == 2 ? (int)cluster_id_x() : (int)blockIdx.x;
+  const int tstep = CG == 2 ? (int)nclusters_x() : (int)gridDim.x;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::kStages; ++s) {
@@ -321,7 +334,7 @@ __global__ void __launch_bounds__(gemm_threads<EW>(), 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], EW);
+      mbar_init(&tempty[a], CG * EW);   // the leader's counts both CTAs' epilogues
     }
     for (int w = 0; w < EW; ++w) mbar_init(&rbar[w], 1);
     fence_barrier_init();
@@ -334,11 +347,19 @@ __global__ void __launch_bounds__(gemm_threads<EW>(), 1)
     if (tma_res) tma_prefetch_desc(&tmRes);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, C::kTmemCols);
-    tmem_relinquish();
+    if (CG == 2) {
+      tmem_alloc_pair(tmem_slot, C::kTmemCols);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, C::kTmemCols);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  // a pair's barriers are signalled across the pair: both CTAs' set-up must
+  // be visible before either starts
+  if (CG == 2) cluster_sync();
+  else __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   // setup above overlaps the previous kernel; its outputs (A, a_scale,
@@ -352,17 +373,27 @@ __global__ void __launch_bounds__(gemm_threads<EW>(), 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
-        const int m0 = (t / num_n) * kBM;
-        const int n0 = (t % num_n) * BN;
+      for (int t = tile0; t < ntiles && ok; t += tstep) {
+        // this CTA's rows of A and of B within the tile
+        const int m0 = (t / num_n) * kBM * CG + (int)rank * kBM;
+        const int n0 = (t % num_n) * BN + (int)rank * (BN / CG);
         for (int kb = 0; kb < nk; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, ICX_DEVICE_TIMEOUT_PRODUCER)) {
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full[stage], C::kStageBytes);
-          tma_load_2d(sA + stage * C::kABytes, &tmA, &full[stage], kb * kBK, m0);
-          tma_load_2d(sB + stage * C::kBBytes, &tmB, &full[stage], kb * kBK, n0);
+          if (CG == 2) {
+            // both CTAs' bytes complete on the leader's barrier; the leader
+            // arrives once, expecting the pair's bytes
+            const uint32_t fb = cluster_addr(&full[stage], 0);
+            if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * C::kStageBytes);
+            tma_load_2d_pair(sA + stage * C::kABytes, &tmA, fb, kb * kBK, m0);
+            tma_load_2d_pair(sB + stage * C::kBBytes, &tmB, fb, kb * kBK, n0);
+          } else {
+            mbar_arrive_expect_tx(&full[stage], C::kStageBytes);
+            tma_load_2d(sA + stage * C::kABytes, &tmA, &full[stage], kb * kBK, m0);
+            tma_load_2d(sB + stage * C::kBBytes, &tmB, &full[stage], kb * kBK, n0);
+          }
           if (++stage == C::kStages) {
             stage = 0;
             phase ^= 1;
@@ -372,13 +403,14 @@ __global__ void __launch_bounds__(gemm_threads<EW>(), 1)
     }
   } else if (warp == 1) {
     // --------------------------------------------------------- MMA issuer
-    if (elect_one()) {
+    // (of a pair, only the leader's: its MMAs cover both CTAs)
+    if ((CG == 1 || rank == 0) && elect_one()) {
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+      for (int t = tile0; t < ntiles && ok; t += tstep) {
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1, ICX_DEVICE_TIMEOUT_MMA)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
@@ -393,17 +425,32 @@ __global__ void __launch_bounds__(gemm_threads<EW>(), 1)
 #pragma unroll
           for (int k = 0; k < kBK / kUmmaK; ++k) {
             // advance the start address by 32 bytes (encoded >> 4) per step
-            mma_i8(d_tmem, da + (uint64_t)(k * 2), db + (uint64_t)(k * 2), idesc,
-                   (kb | k) != 0);
+            if (CG == 2)
+              mma_i8_pair(d_tmem, da + (uint64_t)(k * 2), db + (uint64_t)(k * 2), idesc,
+                          (kb | k) != 0);
+            else
+              mma_i8(d_tmem, da + (uint64_t)(k * 2), db + (uint64_t)(k * 2), idesc,
+                     (kb | k) != 0);
           }
-          mma_commit(&empty[stage]);
+          if (CG == 2) {
+            // the stage is free in both CTAs once these MMAs have read it
+            mma_commit_pair(cluster_addr(&empty[stage], 0));
+            mma_commit_pair(cluster_addr(&empty[stage], 1));
+          } else {
+            mma_commit(&empty[stage]);
+          }
           if (++stage == C::kStages) {
             stage = 0;
             phase ^= 1;
           }
         }
         if (!ok) break;
-        mma_commit(&tfull[acc]);
+        if (CG == 2) {
+          mma_commit_pair(cluster_addr(&tfull[acc], 0));
+          mma_commit_pair(cluster_addr(&tfull[acc], 1));
+        } else {
+          mma_commit(&tfull[acc]);
+        }
         acc ^= 1;
         if (acc == 0) acc_phase ^= 1;
       }
@@ -474,8 +521,8 @@ __global__ void __launch_bounds__(gemm_threads<EW>(), 1)
       __syncwarp();
     };
 
-    for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
-      const int m0 = (t / num_n) * kBM;
+    for (int t = tile0; t < ntiles; t += tstep) {
+      const int m0 = (t / num_n) * kBM * CG + (int)rank * kBM;   // this CTA's 128 rows
       const int n0 = (t % num_n) * BN;
       const int mrow0 = m0 + quad * 32;
       const int m = mrow0 + lane;
@@ -505,7 +552,10 @@ __global__ void __launch_bounds__(gemm_threads<EW>(), 1)
         // the accumulator's columns this warp reads are all in registers
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&tempty[acc]);
+        if (lane == 0) {
+          if (CG == 2) mbar_arrive_cluster(cluster_addr(&tempty[acc], 0));   // the leader's
+          else mbar_arrive(&tempty[acc]);
+        }
         released = true;
       };
 
@@ -763,10 +813,15 @@ __global__ void __launch_bounds__(gemm_threads<EW>(), 1)
   }
 
   tc_fence_before();
-  __syncthreads();
+  __syncwarp();
+  // neither CTA of a pair leaves while the other may still signal its
+  // barriers or the leader's MMAs may still read its shared memory
+  if (CG == 2) cluster_sync();
+  else __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, C::kTmemCols);
+    if (CG == 2) tmem_dealloc_pair(tmem_base, C::kTmemCols);
+    else tmem_dealloc(tmem_base, C::kTmemCols);
   }
 }
 
@@ -886,14 +941,14 @@ static int make_out_tmap(CUtensorMap* map, void* base, size_t M, size_t N, bool 
 
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
-template <int BN, int EPI, bool DEEP, int EW>
+template <int BN, int EPI, bool DEEP, int EW, int CG>
 static int launch_tc(cudaStream_t s, const void* a, bool a_signed, const void* bt,
-                     bool b_signed, const GemmArgs& args) {
-  using C = Cfg<BN, DEEP, EW>;
+                     bool b_signed, const GemmArgs& args, int grid) {
+  using C = Cfg<BN, DEEP, EW, CG>;
   CUtensorMap ta, tb, tout;
   int rc = make_tmap(&ta, a, (size_t)args.M, (size_t)args.K, kBM);
   if (rc) return rc;
-  rc = make_tmap(&tb, bt, (size_t)args.N, (size_t)args.K, BN);
+  rc = make_tmap(&tb, bt, (size_t)args.N, (size_t)args.K, BN / CG);
   if (rc) return rc;
   // TMA stores need a 16-byte aligned base and a row pitch multiple of 16 B
   const int tma_store = C::kOutBufs > 0 && (args.N % 4 == 0) && aligned16(args.out);
@@ -918,20 +973,55 @@ static int launch_tc(cudaStream_t s, const void* a, bool a_signed, const void* b
                            ? 1 | ((args.b_zp && args.b_zp_per_col &&
                                    (reinterpret_cast<uintptr_t>(args.b_zp) & 3) == 0) ? 2 : 0)
                            : 0;
-  auto kern = args.b_zp ? (args.bias ? qgemm_tcgen05_kernel<BN, EPI, true, true, DEEP, EW>
-                                      : qgemm_tcgen05_kernel<BN, EPI, true, false, DEEP, EW>)
-                        : (args.bias ? qgemm_tcgen05_kernel<BN, EPI, false, true, DEEP, EW>
-                                     : qgemm_tcgen05_kernel<BN, EPI, false, false, DEEP, EW>);
+  auto kern = args.b_zp ? (args.bias ? qgemm_tcgen05_kernel<BN, EPI, true, true, DEEP, EW, CG>
+                                      : qgemm_tcgen05_kernel<BN, EPI, true, false, DEEP, EW, CG>)
+                        : (args.bias ? qgemm_tcgen05_kernel<BN, EPI, false, true, DEEP, EW, CG>
+                                     : qgemm_tcgen05_kernel<BN, EPI, false, false, DEEP, EW, CG>);
   ICX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 C::kSmemBytes));
-  const int ntiles = ((args.M + kBM - 1) / kBM) * ((args.N + BN - 1) / BN);
-  int grid = sm_count();
-  if (ntiles < grid) grid = ntiles;
-  const uint32_t idesc = idesc_i8(kBM, BN, a_signed, b_signed);
-  launch_pdl(kern, dim3(grid), dim3(gemm_threads<EW>()), C::kSmemBytes, s, ta, tb, tout, tres, args, idesc, tma_store, vec_cols,
-                                             tma_res);
+  const uint32_t idesc = idesc_i8(kBM * CG, BN, a_signed, b_signed);
+  if (CG == 2)
+    launch_pdl_cluster(kern, dim3(grid), dim3(gemm_threads<EW>()), C::kSmemBytes, s, 2u, ta, tb,
+                       tout, tres, args, idesc, tma_store, vec_cols, tma_res);
+  else
+    launch_pdl(kern, dim3(grid), dim3(gemm_threads<EW>()), C::kSmemBytes, s, ta, tb, tout, tres,
+               args, idesc, tma_store, vec_cols, tma_res);
   ICX_LAUNCH_CHECK();
   return ICX_OK;
+}
+
+// CTA pairs of the cta_group::2 kernels that can be resident at once (every
+// pair kernel runs one CTA per SM, so one query covers them all; cached per
+// device).
+static int max_pair_clusters() {
+  static int cached[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return 0;
+  if (cached[dev]) return cached[dev];
+  using C = Cfg<256, true, 8, 2>;
+  auto kern = qgemm_tcgen05_kernel<256, kEpiF32, false, true, true, 8, 2>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes) !=
+      cudaSuccess)
+    return 0;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * 74);
+  cfg.blockDim = dim3(gemm_threads<8>());
+  cfg.dynamicSmemBytes = C::kSmemBytes;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n < 1) {
+    cudaGetLastError();
+    return 0;
+  }
+  cached[dev] = n;
+  return n;
 }
 
 // Epilogue warps of the shallow (K < 1536) f32 GEMMs: 16 for the GELU
@@ -947,36 +1037,57 @@ static int epilogue_warps(bool gelu) {
   return gelu ? 16 : 8;
 }
 
+// CTA pairs (cta_group::2, 256-row tiles) for large deep GEMMs: half the B
+// bytes per CTA and per MAC, which is what bounds the single-CTA kernel there.
+// ICX_GEMM_PAIR=0|1 forces them off / on (read once, for measurement).
+static int pair_mode() {
+  static int mode = [] {
+    const char* v = getenv("ICX_GEMM_PAIR");
+    return v ? (atoi(v) ? 1 : 0) : -1;
+  }();
+  return mode;
+}
+
 // Which kernel runs a GEMM and with how many CTAs.
 struct GemmPlan {
   int bn;     // 128 / 192 / 256 for the tensor-core kernel, 0 for the SIMT kernel
   int grid;   // CTAs (tensor-core path)
+  int cg;     // 1 (one CTA per tile) or 2 (CTA pairs, 256-row tiles)
 };
 
 static GemmPlan plan_gemm(const GemmArgs& args, const void* a, const void* bt) {
-  GemmPlan p{0, 0};
+  GemmPlan p{0, 0, 1};
   const bool tma_ok = (args.K % 16 == 0) && args.K > 0 &&
                       ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(bt)) & 15) == 0;
   if (!tma_ok) return p;
-  // Tile width: the persistent kernel's time is set by its busiest CTA,
-  // ceil(tiles / SMs) tiles, each costing about BN + 64 (its columns plus the
-  // per-tile A fetch and epilogue overhead, in the same units); take the BN
-  // that minimises that (ties: the wider tile).  E.g. N = 768 at M = 4096
-  // runs 128 tiles of 192 columns (one per CTA) instead of 192 tiles of 128.
   const long sms = sm_count();
-  const long mt = (args.M + kBM - 1) / kBM;
+  const int pm = pair_mode();
+  // (measured: pairs help where the K loop dominates; the shallow GEMMs are
+  // bound by their epilogue and run faster on single CTAs)
+  const bool pair = pm == 1 || (pm < 0 && args.M >= 8192 && args.K >= 1536);
+  const long pairs = pair ? max_pair_clusters() : 0;
+  p.cg = pair && pairs > 0 && args.N > 128 ? 2 : 1;
+  // Tile width: the persistent kernel's time is set by its busiest CTA (or
+  // pair), ceil(tiles / units) tiles, each costing about BN + 64 (its columns
+  // plus the per-tile A fetch and epilogue overhead, in the same units); take
+  // the BN that minimises that (ties: the wider tile).  E.g. N = 768 at
+  // M = 4096 runs 128 tiles of 192 columns (one per CTA) instead of 192
+  // tiles of 128.
+  const long units = p.cg == 2 ? pairs : sms;
+  const long mt = (args.M + kBM * p.cg - 1) / (kBM * p.cg);
   long best = -1;
   for (int bn : {256, 192, 128}) {
+    if (p.cg == 2 && bn == 128) continue;   // pairs run 192- or 256-wide tiles
     const long tiles = mt * ((args.N + bn - 1) / bn);
-    const long cost = ((tiles + sms - 1) / sms) * (bn + 64);
+    const long cost = ((tiles + units - 1) / units) * (bn + 64);
     if (best < 0 || cost < best) {
       best = cost;
       p.bn = bn;
     }
   }
-  if (args.N <= 128) p.bn = 128;
+  if (args.N <= 128) p.bn = 128;   // (single CTA: pairs need N > 128)
   const long tiles = mt * ((args.N + p.bn - 1) / p.bn);
-  p.grid = (int)(tiles < sms ? tiles : sms);
+  p.grid = (int)(tiles < units ? tiles : units) * p.cg;
   return p;
 }
 
@@ -985,6 +1096,21 @@ static int gemm_grid(const GemmArgs& args, const void* a, const void* bt) {
   const GemmPlan p = plan_gemm(args, a, bt);
   if (p.bn) return p.grid;
   return dql_minmax_partials((size_t)args.M * args.N);
+}
+
+// One tile width: single CTAs or CTA pairs (pairs only for 192 / 256
+// columns), a deep ring for K >= 1536, 8 or 16 epilogue warps.
+template <int BN, int EPI>
+static int launch_bn(cudaStream_t s, const void* a, bool a_signed, const void* bt, bool b_signed,
+                     const GemmArgs& args, const GemmPlan& p, bool deep, bool ew16) {
+  constexpr int kEw16 = EPI == kEpiS32 ? 8 : 16;
+  if (p.cg == 2 && BN != 128)
+    return deep   ? launch_tc<BN, EPI, true, 8, (BN == 128 ? 1 : 2)>(s, a, a_signed, bt, b_signed, args, p.grid)
+           : ew16 ? launch_tc<BN, EPI, false, kEw16, (BN == 128 ? 1 : 2)>(s, a, a_signed, bt, b_signed, args, p.grid)
+                  : launch_tc<BN, EPI, false, 8, (BN == 128 ? 1 : 2)>(s, a, a_signed, bt, b_signed, args, p.grid);
+  return deep   ? launch_tc<BN, EPI, true, 8, 1>(s, a, a_signed, bt, b_signed, args, p.grid)
+         : ew16 ? launch_tc<BN, EPI, false, kEw16, 1>(s, a, a_signed, bt, b_signed, args, p.grid)
+                : launch_tc<BN, EPI, false, 8, 1>(s, a, a_signed, bt, b_signed, args, p.grid);
 }
 
 template <int EPI>
@@ -996,18 +1122,9 @@ static int launch_gemm(cudaStream_t s, const void* a, bool a_signed,
   // 16 epilogue warps (more TMEM loads and math in flight) for the shallow
   // GELU GEMM, whose epilogue is the bottleneck; 8 otherwise
   const bool ew16 = !deep && EPI != kEpiS32 && epilogue_warps(EPI == kEpiGelu) == 16;
-  if (p.bn == 256)
-    return deep   ? launch_tc<256, EPI, true, 8>(s, a, a_signed, bt, b_signed, args)
-           : ew16 ? launch_tc<256, EPI, false, (EPI == kEpiS32 ? 8 : 16)>(s, a, a_signed, bt, b_signed, args)
-                  : launch_tc<256, EPI, false, 8>(s, a, a_signed, bt, b_signed, args);
-  if (p.bn == 192)
-    return deep   ? launch_tc<192, EPI, true, 8>(s, a, a_signed, bt, b_signed, args)
-           : ew16 ? launch_tc<192, EPI, false, (EPI == kEpiS32 ? 8 : 16)>(s, a, a_signed, bt, b_signed, args)
-                  : launch_tc<192, EPI, false, 8>(s, a, a_signed, bt, b_signed, args);
-  if (p.bn == 128)
-    return deep   ? launch_tc<128, EPI, true, 8>(s, a, a_signed, bt, b_signed, args)
-           : ew16 ? launch_tc<128, EPI, false, (EPI == kEpiS32 ? 8 : 16)>(s, a, a_signed, bt, b_signed, args)
-                  : launch_tc<128, EPI, false, 8>(s, a, a_signed, bt, b_signed, args);
+  if (p.bn == 256) return launch_bn<256, EPI>(s, a, a_signed, bt, b_signed, args, p, deep, ew16);
+  if (p.bn == 192) return launch_bn<192, EPI>(s, a, a_signed, bt, b_signed, args, p, deep, ew16);
+  if (p.bn == 128) return launch_bn<128, EPI>(s, a, a_signed, bt, b_signed, args, p, deep, ew16);
   const size_t total = (size_t)args.M * args.N;
   const int threads = 256;
   const size_t blocks = (total + threads - 1) / threads;

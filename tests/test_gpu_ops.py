@@ -347,3 +347,48 @@ def test_quant_linear_residual_epilogue_bit_exact():
     out = ops.quant_linear(y, s, z, pw, cu(ws), cu(bias), residual=cu(r))
     ref = oracle.quant_linear(x, w, ws, bias)[0] + r
     np.testing.assert_array_equal(host(out).view(np.uint32), ref.astype(np.float32).view(np.uint32))
+
+
+# Large-M GEMMs (M >= 8192) run as CTA pairs (tcgen05 cta_group::2, 256-row
+# tiles): ragged M and N, per-column scale / zero point, GELU, residual.
+@pytest.mark.parametrize("M,K,N,gelu,per_col,residual", [
+    (8192 + 77, 1024, 1000, False, True, False),
+    (8192 + 200, 768, 1000, True, False, False),
+    (8192, 3072, 768, False, True, True),
+    (16384 - 3, 768, 2304, False, False, True),
+])
+def test_quant_linear_cta_pairs_bit_exact(M, K, N, gelu, per_col, residual):
+    x = synth.normal((M, K), 1.0, 21)
+    w = synth.int8_uniform((K, N), 22)
+    bias = synth.normal((N,), 0.02, 23)
+    if per_col:
+        ws = synth.uniform_f32((N,), 0.005, 0.02, 24)
+        bz = synth.int8_uniform((N,), 25, -8, 8)
+    else:
+        ws, bz = np.array([0.01], np.float32), None
+    res = synth.normal((M, N), 1.0, 26) if residual else None
+    pw = ops.prepare_weight(cu(w))
+    outs = ops.gpu_dynamic_quantize_linear(cu(x), row_len=K if bz is not None else None)
+    y, s, z = outs[:3]
+    rows = outs[3] if bz is not None else None
+    out = ops.quant_linear(y, s, z, pw, cu(ws), cu(bias), None if bz is None else cu(bz), rows,
+                           gelu=gelu, residual=None if res is None else cu(res))
+    ref = oracle.quant_linear_from_q(host(y), host(s).item(), host(z).item(), w, ws, bias, bz,
+                                     gelu=gelu, residual=res, threads=8)
+    ry, rs, rz = oracle.dynamic_quantize_linear(x)
+    np.testing.assert_array_equal(host(y), ry)
+    if gelu:
+        np.testing.assert_allclose(host(out), ref, atol=GELU_ATOL, rtol=0)
+    else:
+        np.testing.assert_array_equal(host(out).view(np.uint32), ref.view(np.uint32))
+
+
+def test_s32_matmul_integer_cta_pairs_bit_exact():
+    M, K, N = 8192 + 5, 1024, 520
+    rng = np.random.default_rng(3)
+    a = rng.integers(0, 256, (M, K)).astype(np.uint8)
+    b = rng.integers(-127, 128, (K, N)).astype(np.int8)
+    az = np.array(9, np.uint8)
+    bz = rng.integers(-8, 9, (N,)).astype(np.int8)
+    got = host(ops.gpu_matmul_integer(cu(a), cu(b), cu(az), cu(bz)))
+    np.testing.assert_array_equal(got, oracle.matmul_integer(a, b, az, bz, threads=8))
