@@ -349,13 +349,14 @@ def test_quant_linear_residual_epilogue_bit_exact():
     np.testing.assert_array_equal(host(out).view(np.uint32), ref.astype(np.float32).view(np.uint32))
 
 
-# Large-M GEMMs (M >= 8192) run as CTA pairs (tcgen05 cta_group::2, 256-row
-# tiles): ragged M and N, per-column scale / zero point, GELU, residual.
+# Large deep GEMMs (M >= 8192, K >= 1536) run as CTA pairs (tcgen05
+# cta_group::2, 256-row tiles): ragged M and N, per-column scale / zero point,
+# GELU, residual.
 @pytest.mark.parametrize("M,K,N,gelu,per_col,residual", [
-    (8192 + 77, 1024, 1000, False, True, False),
-    (8192 + 200, 768, 1000, True, False, False),
+    (8192 + 77, 1536, 1000, False, True, False),
+    (8192 + 200, 2048, 1000, True, False, False),
     (8192, 3072, 768, False, True, True),
-    (16384 - 3, 768, 2304, False, False, True),
+    (16384 - 3, 1536, 2304, False, False, True),
 ])
 def test_quant_linear_cta_pairs_bit_exact(M, K, N, gelu, per_col, residual):
     x = synth.normal((M, K), 1.0, 21)
@@ -384,7 +385,7 @@ def test_quant_linear_cta_pairs_bit_exact(M, K, N, gelu, per_col, residual):
 
 
 def test_s32_matmul_integer_cta_pairs_bit_exact():
-    M, K, N = 8192 + 5, 1024, 520
+    M, K, N = 8192 + 5, 2048, 520
     rng = np.random.default_rng(3)
     a = rng.integers(0, 256, (M, K)).astype(np.uint8)
     b = rng.integers(-127, 128, (K, N)).astype(np.int8)
