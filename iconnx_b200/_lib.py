@@ -48,6 +48,7 @@ PROTOTYPES = {
     "icx_engine_wait": (_i, [_vp, ctypes.c_int64]),
     "icx_nccl_unique_id": (_i, [_vp, _sz]),
     "icx_engine_set_global_dql": (_i, [_vp, _vp, _i, _i]),
+    "icx_engine_abort_global_dql": (_i, [_vp]),
     "icx_engine_output_info": (_i, [_vp, ctypes.c_char_p, _vp, _vp, _vp]),
     "icx_engine_output_copy": (_i, [_vp, ctypes.c_char_p, _vp, _sz]),
     "icx_engine_plan": (ctypes.c_char_p, [_vp]),

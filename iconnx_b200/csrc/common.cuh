@@ -1,7 +1,8 @@
 // Shared device helpers for the iconnx_b200 kernels (sm_100a only).
 //
-// Thin inline-PTX wrappers for mbarriers, TMA (cp.async.bulk.tensor, never
-// with cluster multicast), and the tcgen05 tensor-memory / MMA instructions.
+// Thin inline-PTX wrappers for mbarriers, TMA (cp.async.bulk.tensor, every
+// load into the shared memory of one CTA), and the tcgen05 tensor-memory /
+// MMA instructions.
 // Every spin-wait is bounded: on timeout it records a status code in
 // g_icx_device_status and returns false, so a kernel can unwind instead of
 // hanging the GPU.
@@ -356,8 +357,8 @@ __device__ __forceinline__ void pdl_trigger() {
 // tcgen05 cta_group::2: the even CTA (rank 0, the leader) issues the MMAs,
 // which read A and B from the shared memory of both CTAs at the same
 // offsets and accumulate into the tensor memory of both.  Loads are plain
-// TMA tile loads into each CTA's own shared memory (never multicast); only
-// their completion is counted on the leader's barrier.
+// TMA tile loads, each into its own CTA's shared memory; only their
+// completion is counted on the leader's barrier.
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));

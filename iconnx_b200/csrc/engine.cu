@@ -30,6 +30,7 @@
 #include <nccl.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <cstring>
 #include <functional>
@@ -177,6 +178,7 @@ struct NcclApi {
   ncclResult_t (*all_reduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
                              cudaStream_t) = nullptr;
   ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+  ncclResult_t (*comm_abort)(ncclComm_t) = nullptr;
   const char* (*error_string)(ncclResult_t) = nullptr;
 };
 
@@ -191,9 +193,10 @@ static const NcclApi* nccl_api() {
     api.comm_init_rank = reinterpret_cast<decltype(api.comm_init_rank)>(dlsym(h, "ncclCommInitRank"));
     api.all_reduce = reinterpret_cast<decltype(api.all_reduce)>(dlsym(h, "ncclAllReduce"));
     api.comm_destroy = reinterpret_cast<decltype(api.comm_destroy)>(dlsym(h, "ncclCommDestroy"));
+    api.comm_abort = reinterpret_cast<decltype(api.comm_abort)>(dlsym(h, "ncclCommAbort"));
     api.error_string = reinterpret_cast<decltype(api.error_string)>(dlsym(h, "ncclGetErrorString"));
     ok = api.get_unique_id && api.comm_init_rank && api.all_reduce && api.comm_destroy &&
-         api.error_string;
+         api.comm_abort && api.error_string;
   });
   return ok ? &api : nullptr;
 }
@@ -305,6 +308,8 @@ class Engine {
   int run(const std::vector<std::string>& names, const std::vector<int>& dtypes,
           const std::vector<Shape>& shapes, const std::vector<const void*>& host,
           const std::vector<std::string>& outputs) {
+    ICX_REQUIRE(!collectives_aborted_, "run: this executor's collectives were aborted "
+                "(call set_global_dql again, or build a new executor)");
     int rc = stage_inputs(names, dtypes, shapes, host, outputs);
     if (rc) return rc;
     rc = execute();
@@ -365,6 +370,8 @@ class Engine {
              const std::vector<Shape>& shapes, const std::vector<const void*>& host,
              const std::vector<std::string>& outputs, const std::vector<void*>& host_out,
              const std::vector<size_t>& out_bytes, int64_t* ticket) {
+    ICX_REQUIRE(!collectives_aborted_, "submit: this executor's collectives were aborted "
+                "(call set_global_dql again, or build a new executor)");
     int rc = stage_inputs(names, dtypes, shapes, host, outputs, /*upload=*/false);
     if (rc) return rc;
     if (!copy_stream_) ICX_CUDA(cudaStreamCreateWithFlags(&copy_stream_, cudaStreamNonBlocking));
@@ -467,6 +474,7 @@ class Engine {
   // src/cuda/inference/gpu_event_timer.rs:1-45).
   int profile(std::string* text) {
     ICX_REQUIRE(compiled_, "profile: no compiled plan (call run first)");
+    ICX_REQUIRE(!collectives_aborted_, "profile: this executor's collectives were aborted");
     ICX_CUDA(cudaSetDevice(device_));
     // Every step is captured alone, kReps times in a row, into a CUDA graph
     // and timed with an event pair around its replay: device time only,
@@ -520,6 +528,7 @@ class Engine {
   // run, asynchronously on the engine's stream (no copies, no sync).
   int replay() {
     ICX_REQUIRE(compiled_, "replay: no compiled plan (call run first)");
+    ICX_REQUIRE(!collectives_aborted_, "replay: this executor's collectives were aborted");
     ICX_CUDA(cudaSetDevice(device_));
     return execute();
   }
@@ -541,6 +550,7 @@ class Engine {
   // the arena reuses a slot once its last reader has run).
   int run_step(int i) {
     ICX_REQUIRE(step(i) != nullptr, "run_step: no step %d in the compiled plan", i);
+    ICX_REQUIRE(!collectives_aborted_, "run_step: this executor's collectives were aborted");
     ICX_CUDA(cudaSetDevice(device_));
     int rc = steps_[(size_t)i].fn(stream_);
     if (rc) return rc;
@@ -615,7 +625,7 @@ class Engine {
     }
     if (copy_stream_) cudaStreamDestroy(copy_stream_);
     if (upload_stream_) cudaStreamDestroy(upload_stream_);
-    if (comm_) nccl_api()->comm_destroy(comm_);
+    if (ncclComm_t c = comm_.exchange(nullptr)) nccl_api()->comm_destroy(c);
     if (gdql_) cudaFree(gdql_);
     if (stream_) cudaStreamDestroy(stream_);
   }
@@ -2041,7 +2051,8 @@ class Engine {
   cudaStream_t copy_stream_ = nullptr;
   cudaStream_t upload_stream_ = nullptr;
   int64_t next_ticket_ = 0;
-  ncclComm_t comm_ = nullptr;  // global DQL (set_global_dql)
+  std::atomic<ncclComm_t> comm_{nullptr};  // global DQL (set_global_dql)
+  std::atomic<bool> collectives_aborted_{false};
   float* gdql_ = nullptr;      // (-min, max) pair [0..1] and the (min, max) partial [2..3]
   std::map<int, int> dql_mode_;
   int n_slots_ = 0;
@@ -2068,8 +2079,27 @@ class Engine {
   // batch), so the shards quantise exactly as one executor over the whole
   // batch would.  Every rank must call this concurrently (communicator
   // set-up is collective) and then run the same graph.  nranks <= 1: off.
+  // Aborts the global-DQL communicator (ncclCommAbort): all-reduces of this
+  // executor that wait for a peer that will never join return, instead of
+  // spinning on the GPU forever.  Safe to call from another host thread while
+  // this executor's thread is blocked in run(); touches only the
+  // communicator.  Afterwards run / submit / replay fail until
+  // set_global_dql is called again.
+  int abort_global_dql() {
+    ncclComm_t c = comm_.exchange(nullptr);
+    if (!c) return ICX_OK;
+    collectives_aborted_ = true;
+    const ncclResult_t r = nccl_api()->comm_abort(c);
+    if (r != ncclSuccess) {
+      set_error("ncclCommAbort failed: %s", nccl_api()->error_string(r));
+      return ICX_ERR_CUDA;
+    }
+    return ICX_OK;
+  }
+
   int set_global_dql(const void* id, int nranks, int rank) {
     ICX_CUDA(cudaSetDevice(device_));
+    collectives_aborted_ = false;
     if (comm_) {
       ICX_CUDA(cudaStreamSynchronize(stream_));
       nccl_api()->comm_destroy(comm_);
@@ -2230,6 +2260,11 @@ extern "C" int icx_nccl_unique_id(void* id_out, size_t bytes) {
 extern "C" int icx_engine_set_global_dql(icx_engine* h, const void* nccl_id, int nranks, int rank) {
   ICX_REQUIRE(h, "set_global_dql: null engine");
   return h->e->set_global_dql(nccl_id, nranks, rank);
+}
+
+extern "C" int icx_engine_abort_global_dql(icx_engine* h) {
+  ICX_REQUIRE(h, "abort_global_dql: null engine");
+  return h->e->abort_global_dql();
 }
 
 extern "C" int icx_engine_wait(icx_engine* h, int64_t ticket) {

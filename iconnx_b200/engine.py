@@ -190,6 +190,13 @@ class GpuGraphExecutor:
         buf = ctypes.create_string_buffer(bytes(nccl_id or b""), 128) if nccl_id else None
         check(self._L.icx_engine_set_global_dql(self._h, buf, int(nranks), int(rank)))
 
+    def abort_collectives(self) -> None:
+        """Aborts the global-DQL communicator (ncclCommAbort): all-reduces
+        waiting for a peer that will not join return.  Callable from another
+        thread while this executor's thread is blocked in :meth:`run`; later
+        runs fail until :meth:`set_global_dql` is called again."""
+        check(self._L.icx_engine_abort_global_dql(self._h))
+
     def fetch(self, name: str, out: np.ndarray | None = None) -> np.ndarray:
         dt, rk = ctypes.c_int(), ctypes.c_int()
         dims = (ctypes.c_int64 * 6)()

@@ -15,12 +15,17 @@ shards through one 8-byte NCCL all-reduce (NVLink), and the sharded run is
 bit-equal to one executor over the whole batch.
 
 A failing shard raises in the caller; a shard that does not finish within
-``timeout`` seconds raises TimeoutError without waiting for it.
+``timeout`` seconds raises TimeoutError without waiting for it.  Either way
+the runner is then unusable (a stalled worker may still be driving its
+executor, which is single-threaded), and with ``global_dql`` every
+executor's communicator is aborted first, so that no all-reduce stays
+waiting on a GPU for a shard that will not join.
 """
 
 from __future__ import annotations
 
 import threading
+import time
 from typing import Callable
 
 import numpy as np
@@ -47,7 +52,8 @@ class ShardedRunner:
     """
 
     def __init__(self, build: Callable, devices: list, batch: int,
-                 factory: Callable | None = None, global_dql: bool = False):
+                 factory: Callable | None = None, global_dql: bool = False,
+                 nccl_id: bytes | None = None):
         if factory is None:
             from .engine import GpuGraphExecutor
             factory = GpuGraphExecutor.new
@@ -56,11 +62,14 @@ class ShardedRunner:
         self._build, self._factory = build, factory
         self._ex = [None] * len(self.devices)
         self._nccl_id = None
+        self._broken = None
         if global_dql and len(self.devices) > 1:
             if any(e <= s for s, e in self.bounds):
                 raise ValueError("global_dql needs at least one row per shard")
-            from .engine import nccl_unique_id
-            self._nccl_id = nccl_unique_id()
+            if nccl_id is None:
+                from .engine import nccl_unique_id
+                nccl_id = nccl_unique_id()
+            self._nccl_id = nccl_id
 
     def _ensure(self, i):
         if self._ex[i] is None:
@@ -73,7 +82,22 @@ class ShardedRunner:
             self._ex[i] = ex
         return self._ex[i]
 
+    def _fail(self, why: str) -> None:
+        """Marks the runner unusable and, with global_dql, aborts every
+        executor's communicator so no all-reduce stays waiting for a peer."""
+        self._broken = why
+        if self._nccl_id is not None:
+            for ex in self._ex:
+                if ex is not None:
+                    try:
+                        ex.abort_collectives()
+                    except Exception:  # already aborted / never joined
+                        pass
+
     def run(self, inputs: dict, outputs, timeout: float | None = None) -> dict:
+        if self._broken is not None:
+            raise RuntimeError(f"ShardedRunner is unusable after a failed run ({self._broken}); "
+                               "build a new one")
         n = len(self.devices)
         results: list = [None] * n
         errors: list = [None] * n
@@ -90,12 +114,25 @@ class ShardedRunner:
                    if self.bounds[i][1] > self.bounds[i][0]]
         for t in threads:
             t.start()
+        deadline = None if timeout is None else time.monotonic() + timeout
         for t in threads:
-            t.join(timeout)
+            # one deadline for the whole run; a failed shard ends the wait
+            # early, since with global_dql the others may wait on it forever
+            while t.is_alive():
+                left = None if deadline is None else deadline - time.monotonic()
+                if left is not None and left <= 0:
+                    break
+                t.join(0.05 if left is None else min(0.05, left))
+                if any(e is not None for e in errors):
+                    break
+            if any(e is not None for e in errors):
+                break
             if t.is_alive():
+                self._fail("timeout")
                 raise TimeoutError(f"a shard did not finish within {timeout} s")
         for i, err in enumerate(errors):
             if err is not None:
+                self._fail(f"shard {i} failed")
                 raise RuntimeError(f"shard {i} (device {self.devices[i]}) failed: {err}") from err
         return {o: np.concatenate([r[o] for r in results if r is not None], axis=0) for o in outputs}
 

@@ -294,6 +294,14 @@ ICX_API int icx_engine_wait(icx_engine* e, int64_t ticket);
  * loaded on first use. */
 ICX_API int icx_nccl_unique_id(void* id_out, size_t bytes);
 ICX_API int icx_engine_set_global_dql(icx_engine* e, const void* nccl_id, int nranks, int rank);
+/* Aborts the global-DQL communicator of `e` (ncclCommAbort; no reference
+ * counterpart).  For a sharded run in which one executor failed or stalled:
+ * the other executors' all-reduces would otherwise wait on the GPU for a
+ * peer that never joins.  May be called from another host thread while e's
+ * own thread is blocked in icx_engine_run.  Afterwards run / submit / replay
+ * on e fail with ICX_ERR_INVALID until icx_engine_set_global_dql is called
+ * again. */
+ICX_API int icx_engine_abort_global_dql(icx_engine* e);
 /* The compiled plan, one "op node -> output" line per launch step. */
 ICX_API const char* icx_engine_plan(icx_engine* e);
 /* Replay the compiled plan as a CUDA graph after the first run (default on). */

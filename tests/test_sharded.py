@@ -2,6 +2,7 @@
 host logic of the benchmark, tested on CPU: fake executors that compute,
 fail or stall, and a world_size-2 gloo group for the max-over-ranks timing."""
 import os
+import threading
 import time
 
 import numpy as np
@@ -75,6 +76,52 @@ def test_stalled_shard_times_out_without_hanging():
     with pytest.raises(TimeoutError):
         r.run({"x": np.zeros((4, 2))}, ["y"], timeout=1.0)
     assert time.time() - t0 < 10
+
+
+class _Collective(_Failing):
+    """A fake executor in global-DQL mode: set_global_dql and abort_collectives
+    are recorded; shard 1 fails before its plan runs, shard 2 stalls as an
+    all-reduce would wait for the missing peer (until it is aborted)."""
+    log: list = []
+
+    def set_global_dql(self, nccl_id, nranks, rank):
+        _Collective.log.append(("join", self.dev))
+        self.aborted = threading.Event()
+
+    def abort_collectives(self):
+        _Collective.log.append(("abort", self.dev))
+        self.aborted.set()
+
+    def run(self, inputs, outputs):
+        if self.dev == 1:
+            raise RuntimeError("injected failure before the plan runs")
+        if self.dev == 2:
+            if not self.aborted.wait(20):
+                raise AssertionError("never aborted")
+            raise RuntimeError("all-reduce aborted")
+        return super().run(inputs, outputs)
+
+
+def test_global_dql_failure_aborts_every_shards_collectives():
+    _Collective.log = []
+    r = ShardedRunner(lambda b, n: None, [0, 1, 2], 6, factory=_Collective, global_dql=True,
+                      nccl_id=b"\0" * 128)
+    t0 = time.time()
+    with pytest.raises(RuntimeError, match="shard 1"):
+        r.run({"x": np.zeros((6, 2))}, ["y"], timeout=60)
+    assert time.time() - t0 < 15          # the failure ends the wait, not the timeout
+    aborted = {d for what, d in _Collective.log if what == "abort"}
+    assert {0, 2} <= aborted               # every built executor's communicator
+    with pytest.raises(RuntimeError, match="unusable"):
+        r.run({"x": np.zeros((6, 2))}, ["y"])
+
+
+def test_timeout_marks_runner_unusable():
+    r = ShardedRunner(lambda b, n: None, [0, 1], 4, factory=_Stalling)
+    with pytest.raises(TimeoutError):
+        r.run({"x": np.zeros((4, 2))}, ["y"], timeout=0.5)
+    with pytest.raises(RuntimeError, match="unusable"):
+        r.run({"x": np.zeros((4, 2))}, ["y"])
 
 
 def _rank(rank, world, port, q):
