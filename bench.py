@@ -625,6 +625,27 @@ def run_kernel_probe(args):
     print(f"kernel probe {args.kernel} {args.shape} done", file=sys.stderr)
 
 
+def pin_to_gpu_numa(torch, local):
+    """Restricts this process to the CPU cores NVML reports as closest to its
+    GPU (matched by PCI bus id), so the pinned host buffers of the end-to-end
+    loop are first touched, and later written by the copy engine, in that
+    GPU's NUMA node.  A process-level setting; best effort."""
+    try:
+        import pynvml
+        props = torch.cuda.get_device_properties(local)
+        bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+        pynvml.nvmlInit()
+        h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        words = pynvml.nvmlDeviceGetCpuAffinity(h, (os.cpu_count() + 63) // 64)
+        cpus = {64 * i + b for i, w in enumerate(words) for b in range(64) if (w >> b) & 1}
+        cpus &= set(range(os.cpu_count()))
+        if cpus:
+            os.sched_setaffinity(0, cpus)
+        return len(cpus)
+    except Exception:
+        return None
+
+
 def device_ms(torch, dev, wl, steps, warmup, flush, barrier, clocks=None):
     """Total device time (ms) of `steps` replays of the workload's step, each
     bracketed by CUDA events on the stream the step runs on, with an L2 flush
@@ -712,6 +733,8 @@ def main():
     rank, world, local = dist_env()
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    if world > 1:
+        pin_to_gpu_numa(torch, local)
     pg = None
     if world > 1:
         import torch.distributed as dist

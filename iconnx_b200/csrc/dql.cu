@@ -285,6 +285,134 @@ __global__ void __launch_bounds__(kQuantThreads, 3)
   }
 }
 
+// Row-wise quantise pass: each warp owns whole rows of row_len elements
+// (row_len % 4 == 0, 16-byte aligned x and y) and issues all of a row's
+// 16-byte loads before quantising it (up to 8 per lane in flight), so the
+// per-row sum of y for the weight zero-point correction is a warp reduction
+// and one plain store: no atomics and no zeroing pass.  Same arithmetic as
+// dql_quantize_kernel (quant4 / quant1).
+constexpr int kRowThreads = 256;
+
+__global__ void __launch_bounds__(kRowThreads)
+    dql_quantize_rows_kernel(const float* __restrict__ x, size_t n, size_t nrows, size_t row_len,
+                             const float2* __restrict__ partials, int nparts,
+                             uint8_t* __restrict__ y, float* __restrict__ scale_out,
+                             uint8_t* __restrict__ zp_out, int32_t* __restrict__ rowsum) {
+  pdl_wait();
+  pdl_trigger();
+  const int lane = threadIdx.x & 31;
+  const size_t warp_g = ((size_t)blockIdx.x * kRowThreads + threadIdx.x) >> 5;
+  const size_t nwarps = ((size_t)gridDim.x * kRowThreads) >> 5;
+  const size_t r4 = row_len / 4;  // float4 per row
+  const float4* x4 = reinterpret_cast<const float4*>(x);
+  uint32_t* y4 = reinterpret_cast<uint32_t*>(y);
+  // this warp's first row is requested before the partials are folded
+  constexpr int kU = 8;
+  float4 v[kU];
+  if (warp_g < nrows) {
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const size_t j = (size_t)lane + 32 * u;
+      if (j < r4) v[u] = __ldg(x4 + warp_g * r4 + j);
+    }
+  }
+  DqlParams p;
+  {
+    float mn = 0.0f, mx = 0.0f;
+    for (int i0 = 0; i0 < nparts; i0 += 256) {
+      float2 w[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int i = i0 + 32 * u + lane;
+        w[u] = i < nparts ? partials[i] : make_float2(0.0f, 0.0f);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        mn = fminf(mn, w[u].x);
+        mx = fmaxf(mx, w[u].y);
+      }
+    }
+    warp_minmax(mn, mx);
+    p = dql_params(mn, mx);
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+      *scale_out = (float)p.scale;
+      *zp_out = (uint8_t)p.zpf;
+    }
+  }
+  for (size_t row = warp_g; row < nrows; row += nwarps) {
+    const float4* xr = x4 + row * r4;
+    uint32_t* yr = y4 + row * r4;
+    uint32_t sum = 0;
+    for (size_t j0 = 0; j0 < r4; j0 += 32 * kU) {
+      if (j0 > 0) {
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+          const size_t j = j0 + lane + 32 * u;
+          if (j < r4) v[u] = __ldg(xr + j);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const size_t j = j0 + lane + 32 * u;
+        if (j < r4) {
+          if (rowsum != nullptr) yr[j] = quant4<true>(v[u], p, sum);
+          else yr[j] = quant4<false>(v[u], p, sum);
+        }
+      }
+    }
+    // the next row's first loads go out before this row's sum is reduced
+    const size_t nxt = row + nwarps;
+    if (nxt < nrows) {
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const size_t j = (size_t)lane + 32 * u;
+        if (j < r4) v[u] = __ldg(x4 + nxt * r4 + j);
+      }
+    }
+    if (rowsum != nullptr) {
+      sum = __reduce_add_sync(0xffffffffu, sum);
+      if (lane == 0) rowsum[row] = (int32_t)sum;
+    }
+  }
+  // elements past the last whole row (none when row_len divides n)
+  const size_t done = nrows * row_len;
+  const size_t tid = (size_t)blockIdx.x * kRowThreads + threadIdx.x;
+  const size_t stride = (size_t)gridDim.x * kRowThreads;
+  for (size_t i = done + tid; i < n; i += stride) y[i] = (uint8_t)quant1(__ldg(x + i), p);
+}
+
+// Launches the quantise pass over x with its (min, max) partials: the
+// row-wise kernel when x and y are 16-byte aligned and rows hold a multiple
+// of 4 elements, else the element-wise kernel.
+static int launch_quantize(cudaStream_t s, const float* x, size_t n, const float2* partials,
+                           int nparts, uint8_t* y, float* scale, uint8_t* zp, int32_t* rowsum,
+                           size_t row_len, bool rowsum_zeroed) {
+  const bool aligned = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 15) == 0;
+  // (measured: the row-wise kernel pays off with row sums, whose atomics it
+  // removes; without them the element-wise kernel is faster on small tensors)
+  const size_t rl = row_len;
+  if (rowsum != nullptr && aligned && rl % 4 == 0 && rl > 0) {
+    const size_t nrows = n / rl;
+    size_t blocks = (nrows * 32 + kRowThreads - 1) / kRowThreads;
+    if (blocks > 148 * 8) blocks = 148 * 8;
+    if (blocks < 1) blocks = 1;
+    launch_pdl(dql_quantize_rows_kernel, dim3((unsigned)blocks), dim3(kRowThreads), 0, s, x, n,
+               nrows, rl, partials, nparts, y, scale, zp, rowsum);
+    ICX_LAUNCH_CHECK();
+    return ICX_OK;
+  }
+  if (rowsum && !rowsum_zeroed) ICX_CUDA(cudaMemsetAsync(rowsum, 0, (n / row_len) * sizeof(int32_t), s));
+  const int vec16 = aligned && (rowsum == nullptr || row_len % 4 == 0);
+  size_t work = vec16 ? n / 16 : n;
+  size_t qb = (work + kQuantThreads - 1) / kQuantThreads;
+  if (qb < 1) qb = 1;
+  if (qb > 148 * 3) qb = 148 * 3;
+  launch_pdl(dql_quantize_kernel, dim3((int)qb), dim3(kQuantThreads), 0, s, x, n, partials, nparts, y,
+             scale, zp, rowsum, row_len ? row_len : 1, vec16);
+  ICX_LAUNCH_CHECK();
+  return ICX_OK;
+}
+
 // Global DynamicQuantizeLinear over batch-sharded executors: the local
 // partials fold into one pair (-min, max) so that a single MAX all-reduce
 // across the executors yields the global (min, max) of the whole batch;
@@ -378,18 +506,8 @@ extern "C" int icx_dql_f32_u8(void* stream, const float* d_x, size_t n,
   launch_pdl(dql_minmax_kernel, dim3(blocks), dim3(kMinmaxThreads), 0, s, 
       d_x, n, static_cast<float2*>(d_workspace), d_rowsum, nrows);
   ICX_LAUNCH_CHECK();
-  const bool aligned = ((reinterpret_cast<uintptr_t>(d_x) |
-                         reinterpret_cast<uintptr_t>(d_y)) & 15) == 0;
-  const int vec16 = aligned && (d_rowsum == nullptr || row_len % 4 == 0);
-  size_t work = vec16 ? n / 16 : n;
-  size_t qb = (work + kQuantThreads - 1) / kQuantThreads;
-  if (qb < 1) qb = 1;
-  if (qb > 148 * 3) qb = 148 * 3;
-  launch_pdl(dql_quantize_kernel, dim3((int)qb), dim3(kQuantThreads), 0, s, 
-      d_x, n, static_cast<const float2*>(d_workspace), blocks, d_y, d_scale,
-      d_zp, d_rowsum, row_len ? row_len : 1, vec16);
-  ICX_LAUNCH_CHECK();
-  return ICX_OK;
+  return launch_quantize(s, d_x, n, static_cast<const float2*>(d_workspace), blocks, d_y, d_scale,
+                         d_zp, d_rowsum, row_len, /*rowsum_zeroed=*/true);
 }
 
 extern "C" int icx_dql_quantize_f32_u8(void* stream, const float* d_x, size_t n,
@@ -404,19 +522,8 @@ extern "C" int icx_dql_quantize_f32_u8(void* stream, const float* d_x, size_t n,
   ICX_REQUIRE(d_rowsum == nullptr || (row_len > 0 && n % row_len == 0),
               "DynamicQuantizeLinear: row_len %zu must divide n %zu", row_len, n);
   cudaStream_t s = as_stream(stream);
-  if (d_rowsum) ICX_CUDA(cudaMemsetAsync(d_rowsum, 0, (n / row_len) * sizeof(int32_t), s));
-  const bool aligned = ((reinterpret_cast<uintptr_t>(d_x) |
-                         reinterpret_cast<uintptr_t>(d_y)) & 15) == 0;
-  const int vec16 = aligned && (d_rowsum == nullptr || row_len % 4 == 0);
-  size_t work = vec16 ? n / 16 : n;
-  size_t qb = (work + kQuantThreads - 1) / kQuantThreads;
-  if (qb < 1) qb = 1;
-  if (qb > 148 * 3) qb = 148 * 3;
-  launch_pdl(dql_quantize_kernel, dim3((int)qb), dim3(kQuantThreads), 0, s, 
-      d_x, n, reinterpret_cast<const float2*>(d_minmax), n_minmax, d_y, d_scale, d_zp,
-      d_rowsum, row_len ? row_len : 1, vec16);
-  ICX_LAUNCH_CHECK();
-  return ICX_OK;
+  return launch_quantize(s, d_x, n, reinterpret_cast<const float2*>(d_minmax), n_minmax, d_y,
+                         d_scale, d_zp, d_rowsum, row_len, /*rowsum_zeroed=*/false);
 }
 
 // ---------------------------------------------------------------------------
@@ -491,15 +598,6 @@ extern "C" int icx_dql_f32_u8_noalloc(void* stream, const float* d_x, size_t n,
   const size_t nrows = d_rowsum ? n / row_len : 0;
   launch_pdl(dql_minmax_kernel, dim3(blocks), dim3(kMinmaxThreads), 0, s, d_x, n, scratch, d_rowsum, nrows);
   ICX_LAUNCH_CHECK();
-  const bool aligned = ((reinterpret_cast<uintptr_t>(d_x) |
-                         reinterpret_cast<uintptr_t>(d_y)) & 15) == 0;
-  const int vec16 = aligned && (d_rowsum == nullptr || row_len % 4 == 0);
-  size_t work = vec16 ? n / 16 : n;
-  size_t qb = (work + kQuantThreads - 1) / kQuantThreads;
-  if (qb < 1) qb = 1;
-  if (qb > 148 * 3) qb = 148 * 3;
-  launch_pdl(dql_quantize_kernel, dim3((int)qb), dim3(kQuantThreads), 0, s, 
-      d_x, n, scratch, blocks, d_y, d_scale, d_zp, d_rowsum, row_len ? row_len : 1, vec16);
-  ICX_LAUNCH_CHECK();
-  return ICX_OK;
+  return launch_quantize(s, d_x, n, scratch, blocks, d_y, d_scale, d_zp, d_rowsum, row_len,
+                         /*rowsum_zeroed=*/true);
 }
