@@ -3,10 +3,12 @@
 Restates the reference's legacy CPU GraphExecutor (src/graph_executor.rs:
 92-278: topological order, DynamicQuantizeLinear as a multi-output node
 :203-216, everything else through execute_operator :356-432).  The int8
-operators come from the C++ oracle (oracle.cpp, each citing its reference
-operator); the fp32 glue ops (Gather, LayerNormalization, Softmax, MatMul,
-Transpose, Reshape ...) are plain numpy float32.  The test suite uses it as
-the checker of the GPU engine; the product never imports it.
+operators and the fp32 glue that carries arithmetic (LayerNormalization,
+Softmax, MatMul) come from the C++ oracle (oracle.cpp, each citing its
+reference operator and restating its op order); element-wise Add / Sub /
+Mul / Div are numpy float32 (one IEEE rounding per element, as ndarray's),
+and Gather / Transpose / Reshape / Unsqueeze only move data.  The test suite
+uses it as the checker of the GPU engine; the product never imports it.
 """
 
 from __future__ import annotations
@@ -79,19 +81,16 @@ class CpuGraph:
         if op == "Gather":
             return [np.take(v[0], v[1], axis=0)]
         if op == "LayerNormalization":
-            x = v[0].astype(f32)
-            mean = x.mean(axis=-1, keepdims=True, dtype=f32)
-            var = ((x - mean) ** 2).mean(axis=-1, keepdims=True, dtype=f32)
-            y = (x - mean) / np.sqrt(var + f32(a.get("epsilon", 1e-5))) * v[1]
-            if len(v) > 2 and v[2] is not None:
-                y = y + v[2]
-            return [y.astype(f32)]
+            if a.get("axis", -1) not in (-1, v[0].ndim - 1):
+                raise NotImplementedError("LayerNormalization over a non-last axis")
+            bias = v[2] if len(v) > 2 else None
+            return [oracle.layer_normalization(v[0], v[1], bias, a.get("epsilon", 1e-5))]
         if op == "Softmax":
-            x = v[0]
-            e = np.exp(x - x.max(axis=-1, keepdims=True))
-            return [(e / e.sum(axis=-1, keepdims=True)).astype(f32)]
+            if a.get("axis", -1) not in (-1, v[0].ndim - 1):
+                raise NotImplementedError("Softmax over a non-last axis")
+            return [oracle.softmax(v[0])]
         if op == "MatMul":
-            return [np.matmul(v[0], v[1]).astype(f32)]
+            return [oracle.matmul(v[0], v[1])]
         if op == "Transpose":
             perm = a.get("perm")
             return [np.ascontiguousarray(np.transpose(v[0], perm))]

@@ -15,7 +15,23 @@
 //   src/operators/add.rs:27-85         (f32 broadcast add)
 //   src/operators/erf.rs:30-40         (Abramowitz & Stegun 7.1.26)
 //   src/operators/dequantize_linear.rs:32-179
-//
+// and the fp32 transformer glue around the chain:
+//   src/operators/layer_normalization.rs:25-80
+//   src/operators/softmax.rs:21-56
+//   src/operators/matmul.rs:27-186
+// Those three run on ndarray 0.16 (Cargo.toml:21; no Cargo.lock is vendored,
+// so the resolved patch version is unknown), whose arithmetic this file
+// restates from its published algorithms:
+//   * sum_axis / mean_axis over the contiguous last axis sum each lane with
+//     ndarray's eight-accumulator unrolled fold (numeric_util::unrolled_fold:
+//     p0..p7 take elements i % 8 of every whole group of eight, then
+//     acc = ((((0 + (p0 + p4)) + (p1 + p5)) + (p2 + p6)) + (p3 + p7)), then
+//     the remaining < 8 elements one by one); mean = sum / n;
+//   * Array2::dot of f32 without the blas feature calls matrixmultiply 0.3
+//     sgemm, whose x86-64 FMA kernel accumulates every output over k in
+//     blocks of kc = 256 with one fused multiply-add per step, the first
+//     block stored and later blocks added (c = c + block).
+
 // Build flags matter: -O2 -ffp-contract=off so that no multiply-add pair is
 // fused (Rust never contracts f32 expressions), and no -ffast-math.
 //
@@ -274,6 +290,107 @@ void oracle_quant_linear(const float* x, size_t M, size_t K, const int8_t* W,
   if (sx_out) *sx_out = sx;
   if (zpx_out) *zpx_out = zpx;
   if (acc_out) std::memcpy(acc_out, acc.data(), M * N * sizeof(int32_t));
+}
+
+// ------------------------------------------------------------ fp32 glue
+// ndarray's unrolled_fold(xs, 0, +) on n contiguous floats (see header).
+static float sum_unrolled8(const float* x, size_t n) {
+  float p[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  size_t i = 0;
+  for (; i + 8 <= n; i += 8)
+    for (int u = 0; u < 8; ++u) p[u] = p[u] + x[i + u];
+  float acc = 0.0f;
+  acc = acc + (p[0] + p[4]);
+  acc = acc + (p[1] + p[5]);
+  acc = acc + (p[2] + p[6]);
+  acc = acc + (p[3] + p[7]);
+  for (; i < n; ++i) acc = acc + x[i];
+  return acc;
+}
+
+float oracle_sum_f32(const float* x, size_t n) { return sum_unrolled8(x, n); }
+
+// LayerNormalization over the last axis.  layer_normalization.rs:25-80:
+// mean = mean_axis(x); centered = x - mean; variance = mean_axis(centered^2);
+// std = sqrt(variance + epsilon); y = (centered / std) * scale + bias, every
+// step its own f32 rounding.
+void oracle_layernorm(const float* x, size_t rows, size_t D, const float* scale,
+                      const float* bias, float eps, float* y) {
+  std::vector<float> c(D), c2(D);
+  const float n = (float)D;
+  for (size_t r = 0; r < rows; ++r) {
+    const float* xr = x + r * D;
+    const float mean = sum_unrolled8(xr, D) / n;
+    for (size_t i = 0; i < D; ++i) c[i] = xr[i] - mean;
+    for (size_t i = 0; i < D; ++i) c2[i] = c[i] * c[i];
+    const float var = sum_unrolled8(c2.data(), D) / n;
+    const float sd = std::sqrt(var + eps);
+    for (size_t i = 0; i < D; ++i) {
+      const float normalized = c[i] / sd;
+      const float scaled = normalized * scale[i];
+      y[r * D + i] = scaled + (bias ? bias[i] : 0.0f);
+    }
+  }
+}
+
+// Softmax over the last axis.  softmax.rs:43-56: max (fold from -inf),
+// shifted = x - max, e = exp(shifted) (the platform libm, as Rust's f32::exp),
+// sum = sum_axis(e), y = e / sum.
+void oracle_softmax(const float* x, size_t rows, size_t D, float* y) {
+  std::vector<float> e(D);
+  for (size_t r = 0; r < rows; ++r) {
+    const float* xr = x + r * D;
+    float mx = -INFINITY;
+    for (size_t i = 0; i < D; ++i) mx = std::fmax(mx, xr[i]);
+    for (size_t i = 0; i < D; ++i) e[i] = std::exp(xr[i] - mx);
+    const float sum = sum_unrolled8(e.data(), D);
+    for (size_t i = 0; i < D; ++i) y[r * D + i] = e[i] / sum;
+  }
+}
+
+// One [M, K] x [K, N] product the way matrixmultiply's FMA sgemm kernel
+// accumulates it (see header): per output, k in blocks of 256, a fused
+// multiply-add per step, block sums added in order.
+}  // extern "C"
+
+template <bool HW_FMA>
+static void matmul_blocks(const float* a, const float* b, size_t M, size_t K, size_t N,
+                          float* c) {
+  constexpr size_t kKC = 256;
+  for (size_t i = 0; i < M; ++i)
+    for (size_t j = 0; j < N; ++j) {
+      float out = 0.0f;
+      for (size_t k0 = 0; k0 < K || k0 == 0; k0 += kKC) {
+        float acc = 0.0f;
+        const size_t k1 = k0 + kKC < K ? k0 + kKC : K;
+        for (size_t k = k0; k < k1; ++k)
+          acc = HW_FMA ? __builtin_fmaf(a[i * K + k], b[k * N + j], acc)
+                       : std::fma(a[i * K + k], b[k * N + j], acc);
+        out = k0 == 0 ? acc : out + acc;
+        if (K == 0) break;
+      }
+      c[i * N + j] = out;
+    }
+}
+
+__attribute__((target("fma"))) static void matmul_blocks_fma(const float* a, const float* b,
+                                                             size_t M, size_t K, size_t N,
+                                                             float* c) {
+  matmul_blocks<true>(a, b, M, K, N, c);
+}
+
+extern "C" {
+
+// MatMul, batched over `batch` pairs of contiguous matrices (matmul.rs:
+// 118-176: each batch's [M, K] and [K, N] slice through Array2::dot; a
+// stride of 0 broadcasts that operand).
+void oracle_matmul(const float* a, const float* b, size_t batch, size_t M, size_t K, size_t N,
+                   size_t a_stride, size_t b_stride, float* c) {
+  static const bool hw = __builtin_cpu_supports("fma");
+  for (size_t t = 0; t < batch; ++t) {
+    if (hw) matmul_blocks_fma(a + t * a_stride, b + t * b_stride, M, K, N, c + t * M * N);
+    else matmul_blocks<false>(a + t * a_stride, b + t * b_stride, M, K, N, c + t * M * N);
+  }
 }
 
 int oracle_max_threads(void) {

@@ -46,6 +46,11 @@ def lib() -> ctypes.CDLL:
         L.oracle_quant_linear.argtypes = [vp, sz, sz, vp, sz, vp, ctypes.c_int, vp, ctypes.c_int,
                                           vp, ctypes.c_int, vp, vp, vp, vp, vp, ctypes.c_int]
         L.oracle_max_threads.restype = ctypes.c_int
+        L.oracle_sum_f32.argtypes = [vp, sz]
+        L.oracle_sum_f32.restype = ctypes.c_float
+        L.oracle_layernorm.argtypes = [vp, sz, sz, vp, vp, f32, vp]
+        L.oracle_softmax.argtypes = [vp, sz, sz, vp]
+        L.oracle_matmul.argtypes = [vp, vp, sz, sz, sz, sz, sz, sz, vp]
         _lib = L
     return _lib
 
@@ -163,6 +168,51 @@ def quant_linear(x: np.ndarray, w: np.ndarray, w_scale, bias: np.ndarray, b_zp=N
     lib().oracle_quant_linear(_p(x2), M, K, _p(w), N, _p(ws), int(ws.size > 1), _p(bz), bz_pc,
                               _p(bias), int(gelu), _p(out), _p(q), _p(s), _p(z), _p(acc), threads)
     return out, q, np.float32(s[0]), np.uint8(z[0]), acc
+
+
+def sum_f32(x: np.ndarray) -> np.float32:
+    """ndarray's unrolled eight-accumulator sum of a contiguous f32 lane."""
+    x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1)
+    return np.float32(lib().oracle_sum_f32(_p(x), x.size))
+
+
+def layer_normalization(x: np.ndarray, scale: np.ndarray, bias=None, epsilon: float = 1e-5):
+    """LayerNormalization over the last axis (layer_normalization.rs:25-80)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    D = x.shape[-1]
+    y = np.empty_like(x)
+    sc = np.ascontiguousarray(scale, dtype=np.float32).reshape(-1)
+    bi = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32).reshape(-1)
+    lib().oracle_layernorm(_p(x), x.size // D if D else 0, D, _p(sc), _p(bi),
+                           ctypes.c_float(float(np.float32(epsilon))), _p(y))
+    return y
+
+
+def softmax(x: np.ndarray) -> np.ndarray:
+    """Softmax over the last axis (softmax.rs:21-56)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    D = x.shape[-1]
+    y = np.empty_like(x)
+    lib().oracle_softmax(_p(x), x.size // D if D else 0, D, _p(y))
+    return y
+
+
+def matmul(a: np.ndarray, b: np.ndarray) -> np.ndarray:
+    """MatMul of rank >= 2 operands with equal or absent batch dimensions
+    (matmul.rs:27-186, ndarray / matrixmultiply arithmetic)."""
+    a = np.ascontiguousarray(a, dtype=np.float32)
+    b = np.ascontiguousarray(b, dtype=np.float32)
+    M, K = a.shape[-2:]
+    K2, N = b.shape[-2:]
+    assert K == K2, "inner dimensions must match"
+    ab, bb = a.shape[:-2], b.shape[:-2]
+    if ab and bb and ab != bb:
+        raise ValueError(f"batch dimensions must match: {ab} vs {bb}")
+    out_batch = ab if ab else bb
+    batch = int(np.prod(out_batch)) if out_batch else 1
+    c = np.empty((*out_batch, M, N), dtype=np.float32)
+    lib().oracle_matmul(_p(a), _p(b), batch, M, K, N, M * K if ab else 0, K * N if bb else 0, _p(c))
+    return c
 
 
 def max_threads() -> int:

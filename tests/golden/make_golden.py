@@ -35,6 +35,19 @@ CASES = [
     "test_erf",
     "test_gelu_default_1",
     "test_gelu_default_2",
+    # the fp32 glue of the encoder (last-axis forms, the ones the reference's
+    # single-axis LayerNormalization / Softmax implement)
+    "test_layer_normalization_2d_axis_negative_1",
+    "test_layer_normalization_3d_axis_negative_1_epsilon",
+    "test_layer_normalization_4d_axis_negative_1",
+    "test_softmax_axis_2",
+    "test_softmax_default_axis",
+    "test_softmax_example",
+    "test_softmax_large_number",
+    "test_softmax_negative_axis",
+    "test_matmul_2d",
+    "test_matmul_3d",
+    "test_matmul_4d",
 ]
 
 # ONNX TensorProto.DataType -> numpy dtype
@@ -112,6 +125,57 @@ def decode_tensor(buf: bytes) -> dict:
             "shape": list(arr.shape), "data": _jsonable(arr)}
 
 
+def _fields(buf: bytes):
+    """(field, wire, value) of one protobuf message; length-delimited values
+    as bytes, fixed32 as raw 4 bytes."""
+    i = 0
+    while i < len(buf):
+        key, i = _varint(buf, i)
+        field, wire = key >> 3, key & 7
+        if wire == 0:
+            v, i = _varint(buf, i)
+        elif wire == 2:
+            ln, i = _varint(buf, i)
+            v = buf[i:i + ln]
+            i += ln
+        elif wire == 5:
+            v = buf[i:i + 4]
+            i += 4
+        elif wire == 1:
+            v = buf[i:i + 8]
+            i += 8
+        else:
+            raise ValueError(f"unsupported wire type {wire}")
+        yield field, wire, v
+
+
+def decode_attributes(model: bytes) -> dict:
+    """Scalar attributes (int / float) of the model's nodes: ModelProto.graph
+    (7) -> GraphProto.node (1) -> NodeProto.attribute (5) -> AttributeProto
+    name (1), f (2), i (3)."""
+    out = {}
+    for f7, _, graph in _fields(model):
+        if f7 != 7:
+            continue
+        for f1, _, node in _fields(graph):
+            if f1 != 1:
+                continue
+            for f5, _, attr in _fields(node):
+                if f5 != 5:
+                    continue
+                name, val = None, None
+                for fa, wa, v in _fields(attr):
+                    if fa == 1:
+                        name = v.decode()
+                    elif fa == 2 and wa == 5:
+                        val = struct.unpack("<f", v)[0]
+                    elif fa == 3 and wa == 0:
+                        val = v - (1 << 64) if v >= (1 << 63) else v
+                if name is not None and val is not None:
+                    out[name] = val
+    return out
+
+
 def _jsonable(arr: np.ndarray) -> list:
     if arr.dtype == np.float32:
         # store exact bit patterns so the fixtures are lossless
@@ -134,6 +198,10 @@ def main(ref_root: str) -> None:
                 with open(os.path.join(ds, f"{kind}_{idx}.pb"), "rb") as f:
                     entry[kind + "s"].append(decode_tensor(f.read()))
                 idx += 1
+        with open(os.path.join(node_dir, case, "model.onnx"), "rb") as f:
+            attrs = decode_attributes(f.read())
+        if attrs:
+            entry["attributes"] = attrs
         with open(os.path.join(out_dir, case + ".json"), "w") as f:
             json.dump(entry, f, indent=1)
         print(case, [t["shape"] for t in entry["inputs"]],

@@ -20,3 +20,9 @@ def load(case):
     with open(os.path.join(GOLDEN, case + ".json")) as f:
         e = json.load(f)
     return [_arr(t) for t in e["inputs"]], [_arr(t) for t in e["outputs"]]
+
+
+def attributes(case):
+    """Scalar node attributes recorded with the fixture (may be empty)."""
+    with open(os.path.join(GOLDEN, case + ".json")) as f:
+        return json.load(f).get("attributes", {})

@@ -6,12 +6,15 @@ Known answers restated from (reference paths):
   src/operators/matmul_integer.rs:273-382
   src/operators/dequantize_linear.rs:216-297
   src/operators/erf.rs:42-171
+  tests/operators/layer_norm_test.rs, softmax_test.rs, matmul_test.rs (the
+  fp32 glue of the encoder, restated from src/operators/
+  layer_normalization.rs:25-80, softmax.rs:21-56, matmul.rs:27-186)
 """
 import numpy as np
 import pytest
 
 from oracle import oracle
-from tests.golden_io import load
+from tests.golden_io import attributes, load
 
 
 # --- DynamicQuantizeLinear KATs (dynamic_quantize_linear.rs:119-169) -------
@@ -162,3 +165,101 @@ def test_quant_linear_chain_composes_ops():
     sc = np.float32(s2) * np.float32(0.01)
     ref = oracle.gelu(oracle.cast_i32_f32(acc2) * sc + bias)
     np.testing.assert_array_equal(out, ref)
+
+
+
+# --- fp32 glue: reference KATs and ONNX node vectors -------------------------
+def test_layer_norm_reference_kats():
+    # tests/operators/layer_norm_test.rs: rows normalise to mean ~0; with
+    # scale 2 and bias 1 the mean is ~1
+    y = oracle.layer_normalization(np.array([[1, 2, 3, 4]], np.float32), np.ones(4, np.float32),
+                                   np.zeros(4, np.float32))
+    assert abs(y.mean()) < 0.01
+    y = oracle.layer_normalization(np.array([[1, 2, 3], [4, 5, 6]], np.float32),
+                                   np.ones(3, np.float32), np.zeros(3, np.float32))
+    assert np.all(np.abs(y.mean(-1)) < 0.01)
+    y = oracle.layer_normalization(np.array([[1, 2, 3]], np.float32), np.full(3, 2, np.float32),
+                                   np.ones(3, np.float32))
+    assert abs(y.mean() - 1.0) < 0.1
+
+
+def test_layer_norm_op_order_is_the_references():
+    """mean -> centered -> variance -> sqrt(var + eps) -> divide -> scale ->
+    bias, each rounded once, sums in ndarray's 8-accumulator order."""
+    x = (np.arange(19, dtype=np.float32) * np.float32(0.37) - np.float32(2.1)).reshape(1, 19)
+    g = np.linspace(0.5, 1.5, 19).astype(np.float32)
+    b = np.linspace(-0.1, 0.1, 19).astype(np.float32)
+    f32 = np.float32
+
+    def s8(v):
+        p = [f32(0)] * 8
+        n8 = len(v) // 8 * 8
+        for i in range(0, n8, 8):
+            for u in range(8):
+                p[u] = f32(p[u] + v[i + u])
+        acc = f32(0)
+        for u in range(4):
+            acc = f32(acc + f32(p[u] + p[u + 4]))
+        for t in v[n8:]:
+            acc = f32(acc + t)
+        return acc
+
+    r = x[0]
+    mean = f32(s8(r) / f32(19))
+    c = (r - mean).astype(f32)
+    var = f32(s8((c * c).astype(f32)) / f32(19))
+    sd = f32(np.sqrt(f32(var + f32(1e-5))))
+    want = (((c / sd).astype(f32) * g).astype(f32) + b).astype(f32)
+    got = oracle.layer_normalization(x, g, b, 1e-5)[0]
+    np.testing.assert_array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+@pytest.mark.parametrize("case", ["test_layer_normalization_2d_axis_negative_1",
+                                  "test_layer_normalization_3d_axis_negative_1_epsilon",
+                                  "test_layer_normalization_4d_axis_negative_1"])
+def test_layer_norm_onnx_golden(case):
+    (x, scale, bias), (y, *_) = load(case)
+    eps = attributes(case).get("epsilon", 1e-5)
+    np.testing.assert_allclose(oracle.layer_normalization(x, scale, bias, eps), y,
+                               rtol=1e-5, atol=1e-6)
+
+
+def test_softmax_reference_kats():
+    # tests/operators/softmax_test.rs: [1, 2, 3] -> ~[0.090, 0.245, 0.665]
+    y = oracle.softmax(np.array([1, 2, 3], np.float32))
+    assert abs(y.sum() - 1.0) < 1e-3
+    np.testing.assert_allclose(y, [0.090, 0.245, 0.665], atol=0.01)
+
+
+@pytest.mark.parametrize("case", ["test_softmax_axis_2", "test_softmax_default_axis",
+                                  "test_softmax_example", "test_softmax_large_number",
+                                  "test_softmax_negative_axis"])
+def test_softmax_onnx_golden(case):
+    (x,), (y,) = load(case)
+    np.testing.assert_allclose(oracle.softmax(x), y, rtol=1e-6, atol=1e-7)
+
+
+@pytest.mark.parametrize("case", ["test_matmul_2d", "test_matmul_3d", "test_matmul_4d"])
+def test_matmul_onnx_golden(case):
+    (a, b), (y,) = load(case)
+    np.testing.assert_allclose(oracle.matmul(a, b), y, rtol=1e-6, atol=1e-6)
+
+
+def test_matmul_blocks_of_256_fused_steps():
+    """matrixmultiply's FMA kernel: one fused multiply-add per k, blocks of
+    kc = 256 summed in order (restated, not numpy's BLAS order)."""
+    rng = np.random.default_rng(5)
+    a = rng.standard_normal((3, 600)).astype(np.float32)
+    b = rng.standard_normal((600, 2)).astype(np.float32)
+    want = np.empty((3, 2), np.float32)
+    for i in range(3):
+        for j in range(2):
+            out = None
+            for k0 in range(0, 600, 256):
+                acc = np.float64(0)
+                for k in range(k0, min(k0 + 256, 600)):
+                    # one rounding per fused step: exact product + acc, then f32
+                    acc = np.float64(np.float32(np.float64(a[i, k]) * np.float64(b[k, j]) + acc))
+                out = np.float32(acc) if out is None else np.float32(out + np.float32(acc))
+            want[i, j] = out
+    np.testing.assert_array_equal(oracle.matmul(a, b).view(np.uint32), want.view(np.uint32))
