@@ -1024,17 +1024,18 @@ static int max_pair_clusters() {
   return n;
 }
 
-// Epilogue warps of the shallow (K < 1536) f32 GEMMs: 16 for the GELU
-// variant, 8 for the others; ICX_GEMM_EPI_WARPS=8|16 overrides both (read
-// once per process, for measurement).
-static int epilogue_warps(bool gelu) {
+// Epilogue warps of the shallow (K < 1536) f32 GEMMs: 16 (the epilogue is
+// their bottleneck and more warps in flight hide its TMEM and store
+// latencies; measured faster than 8 for the GELU and the QKV GEMMs, equal for
+// the residual ones); ICX_GEMM_EPI_WARPS=8 forces 8 (read once per process,
+// for measurement).
+static int epilogue_warps() {
   static int forced = [] {
     const char* v = getenv("ICX_GEMM_EPI_WARPS");
     const int n = v ? atoi(v) : 0;
     return n == 8 || n == 16 ? n : 0;
   }();
-  if (forced) return forced;
-  return gelu ? 16 : 8;
+  return forced ? forced : 16;
 }
 
 // CTA pairs (cta_group::2, 256-row tiles) for large deep GEMMs: half the B
@@ -1119,9 +1120,7 @@ static int launch_gemm(cudaStream_t s, const void* a, bool a_signed,
   if (args.M == 0 || args.N == 0) return ICX_OK;
   const GemmPlan p = plan_gemm(args, a, bt);
   const bool deep = args.K >= 1536;
-  // 16 epilogue warps (more TMEM loads and math in flight) for the shallow
-  // GELU GEMM, whose epilogue is the bottleneck; 8 otherwise
-  const bool ew16 = !deep && EPI != kEpiS32 && epilogue_warps(EPI == kEpiGelu) == 16;
+  const bool ew16 = !deep && EPI != kEpiS32 && epilogue_warps() == 16;
   if (p.bn == 256) return launch_bn<256, EPI>(s, a, a_signed, bt, b_signed, args, p, deep, ew16);
   if (p.bn == 192) return launch_bn<192, EPI>(s, a, a_signed, bt, b_signed, args, p, deep, ew16);
   if (p.bn == 128) return launch_bn<128, EPI>(s, a, a_signed, bt, b_signed, args, p, deep, ew16);
