@@ -14,7 +14,10 @@ oracle restatement of the reference operators:
   bit-exact on sampled rows (first and last included) - MatMulInteger, Cast,
   Mul, Add and the residual Add each rounded as the reference's CPU
   GraphExecutor does (graph_executor.rs:92-278);
-* QuantLinear+GELU: within the GELU tolerance (1e-5 absolute).
+* QuantLinear+GELU: within the GELU tolerance (1e-5 absolute);
+* LayerNormalization: bit-exact on sampled rows against the restated
+  reference operator (layer_normalization.rs:25-80, its op order and sum
+  order).
 """
 from __future__ import annotations
 
@@ -45,7 +48,7 @@ def _weight(inits: dict, name: str) -> np.ndarray:
     return inits[name]
 
 
-def check_plan(ex, inits: dict, rows: int = 64, threads: int = 8) -> dict:
+def check_plan(ex, inits: dict, rows: int = 64, threads: int = 8, attrs: dict | None = None) -> dict:
     """Re-runs the executor's compiled plan step by step and checks every
     int8 stage against the oracle.  ``inits`` maps initializer names to the
     arrays the graph was built with.  Returns per-kind counts of checked
@@ -98,6 +101,22 @@ def check_plan(ex, inits: dict, rows: int = 64, threads: int = 8) -> dict:
                     f"step {i} {op} {node}: {len(bad)} f32 values differ; row {r[m]} col {n}: "
                     f"{got[m, n]!r} != {ref[m, n]!r}")
             counts[op] = counts.get(op, 0) + 1
+        elif op == "LayerNormalization":
+            xn, gn, bn = (info["in"].split(",") + ["", ""])[:3]
+            x = ex.value(xn)
+            D = x.shape[-1]
+            x = x.reshape(-1, D)
+            r = sample_rows(x.shape[0], rows, seed=i)
+            ex.run_step(i)
+            got = ex.value(info["outs"].split(",")[0]).reshape(-1, D)[r]
+            eps = (attrs or {}).get(node, {}).get("epsilon", 1e-5)
+            ref = oracle.layer_normalization(x[r], inits[gn], inits[bn] if bn else None, eps)
+            if not np.array_equal(got.view(np.uint32), ref.view(np.uint32)):
+                bad = np.argwhere(got.view(np.uint32) != ref.view(np.uint32))
+                m, n = bad[0]
+                raise AssertionError(f"step {i} {op} {node}: {len(bad)} values differ; row {r[m]} "
+                                     f"col {n}: {got[m, n]!r} != {ref[m, n]!r}")
+            counts["layernorm"] = counts.get("layernorm", 0) + 1
         else:
             ex.run_step(i)
             counts["other"] = counts.get("other", 0) + 1

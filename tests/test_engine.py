@@ -247,3 +247,25 @@ def test_submit_wait_pipeline_equals_run():
         ex.wait(t)
     for h, r in zip(hosts, ref):
         np.testing.assert_array_equal(h.view(np.uint32), r.view(np.uint32))
+
+
+@gpu
+@pytest.mark.parametrize("rows,D,eps", [(4096, 768, 1e-12), (37, 768, 1e-5), (256, 100, 0.1)])
+def test_layernorm_bit_exact_with_the_reference_operator(rows, D, eps):
+    """LayerNormalization on the GPU follows the reference's op order and sum
+    order (src/operators/layer_normalization.rs:25-80, ndarray's lane sums),
+    so the whole tensor matches the restated operator bit for bit."""
+    from iconnx_b200.engine import GpuGraphExecutor
+    from oracle import oracle
+    gamma = (1.0 + synth.normal((D,), 0.02, 61)).astype(np.float32)
+    beta = synth.normal((D,), 0.02, 62)
+    ex = GpuGraphExecutor.new()
+    ex.add_input("x", [rows, D])
+    ex.add_initializer("g", gamma)
+    ex.add_initializer("b", beta)
+    ex.add_node("ln", "LayerNormalization", ["x", "g", "b"], ["y"], {"axis": -1, "epsilon": eps})
+    x = synth.normal((rows, D), 3.0, 63) + np.float32(0.5)
+    x[0, :] = np.float32(1.25)          # a constant row: zero variance, zero centred values
+    got = ex.run({"x": x}, ["y"])["y"]
+    ref = oracle.layer_normalization(x, gamma, beta, eps)
+    np.testing.assert_array_equal(got.view(np.uint32), ref.view(np.uint32))

@@ -3,6 +3,9 @@ the benchmark configurations (the plans bench.py times: QKV merged, residual
 Adds fused, producer-fused (min, max) with quantise-only DynamicQuantizeLinear,
 CUDA-graph replay), against the oracle restatement of the reference operators.
 
+LayerNormalization steps are bit-exact too (the kernel follows the
+reference's op order and sum order).
+
 Reference paths: GraphExecutor::run (src/graph_executor.rs:92-278) and
 GpuGraphExecutor::run (src/cuda/inference/mod.rs:428-464).  Each int8 stage
 gets its own GPU inputs (tests/stage_parity.py), so an fp32 glue difference
@@ -24,6 +27,7 @@ def _build(build, *args):
     ex, rec = GpuGraphExecutor.new(), CpuGraph()
     out = build(ex, *args)
     build(rec, *args)
+    ex.node_attrs = {name: attrs for name, _, _, _, attrs in rec.nodes}
     return ex, rec.inits, out
 
 
@@ -31,7 +35,7 @@ def _run_and_check(ex, inits, inp, out):
     first = ex.run(inp, [out])[out]
     second = ex.run(inp, [out])[out]          # captured-graph replay
     np.testing.assert_array_equal(first.view(np.uint32), second.view(np.uint32))
-    counts = check_plan(ex, inits)
+    counts = check_plan(ex, inits, attrs=getattr(ex, "node_attrs", None))
     # the step-by-step re-execution reproduces the run bit for bit
     np.testing.assert_array_equal(ex.fetch(out).view(np.uint32), first.view(np.uint32))
     return counts
@@ -58,6 +62,7 @@ def test_config3_distilbert_plan_stage_by_stage():
     assert counts["QuantLinear(QKV)"] == L
     assert counts["QuantLinear+Residual"] == 2 * L
     assert counts["QuantLinear+GELU"] == L
+    assert counts["layernorm"] == 2 * L + 1
 
 
 @gpu
@@ -72,6 +77,7 @@ def test_config4_bert_base_plan_stage_by_stage():
     assert counts["QuantLinear(QKV)"] == L
     assert counts["QuantLinear+Residual"] == 2 * L
     assert counts["QuantLinear+GELU"] == L
+    assert counts["layernorm"] == 2 * L + 1
 
 
 @gpu
