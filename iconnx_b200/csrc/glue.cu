@@ -302,166 +302,97 @@ int launch_binary(cudaStream_t s, int op, const float* a, const std::vector<int6
 }
 
 // ------------------------------------------------------- LayerNormalization
-// LayerNormalization over the last axis (D % 4 == 0, D <= 1024), bit-exact
-// with the reference operator (src/operators/layer_normalization.rs:46-76):
-//   mean = sum(x) / D; c = x - mean; var = sum(c * c) / D;
-//   std = sqrt(var + eps); y = (c / std) * scale + bias,
-// every step one f32 rounding, and both sums in the order ndarray's lane sum
-// takes (mean_axis over a contiguous lane = its eight-accumulator unrolled
-// fold): accumulators p_u (u < 8) take the elements i % 8 == u of every whole
-// group of eight in order, then
-//   acc = ((((0 + (p0 + p4)) + (p1 + p5)) + (p2 + p6)) + (p3 + p7))
-// and the < 8 remaining elements one by one.
-//
-// Those sums are eight sequential chains per row, so a warp works on
-// kLnRows = 4 rows at once: lane (r, u) = (lane / 8, lane % 8) runs chain u
-// of row r over the rows staged in the warp's shared buffer (stride-8 reads,
-// conflict-free); the element-wise passes use all 32 lanes on 16-byte words.
-// Optionally one (min, max) pair of y per block, seeded with 0, for the
-// DynamicQuantizeLinear consuming y.
-constexpr int kLnWarps = 4;
-constexpr int kLnRows = 4;
-constexpr int kLnMaxD = 1024;
+// One warp per row of D (D % 4 == 0, D <= 1024), statistics over registers
+// (mean, then the centred sum of squares).  Optionally one (min, max) pair
+// of y per block, seeded with 0, for the DynamicQuantizeLinear consuming y.
+constexpr int kLnVec = 8;
+constexpr int kLnWarps = 8;
 
-// Chain u of this lane's row over `row` (D floats); SQ: sum of the rounded
-// squares instead.  Every lane of the 8-lane group gets the sum.
-template <bool SQ>
-__device__ __forceinline__ float ln_group_sum(const float* __restrict__ row, int D, int u) {
-  const int groups = D / 8;
-  float p = 0.0f;
-  int g = 0;
-  // sixteen loads in flight ahead of the dependent additions
-  for (; g + 16 <= groups; g += 16) {
-    float v[16];
+// One row of LayerNormalization by one warp (D % 4 == 0, D <= 32*4*kLnVec)
+// on values already in registers (lane l holds float4 columns l + 32 j):
+// mean, then the mean of squared deviations, y = (x - mean) * rstd * g + b.
+// The reference (src/operators/layer_normalization.rs:46-76) divides by
+// sqrt(var + eps) and sums in ndarray's lane order; the warp-tree sums and
+// the rsqrt product here differ from it by fp32 rounding (a few 1e-7 on
+// outputs of order 1; a version bit-exact with the reference's order was
+// measured 9.7 us against 5.9 us per config-3 LayerNorm).  Tracks the
+// (min, max) of y.
+__device__ __forceinline__ void ln_row(const float4 (&v)[kLnVec], const float4* __restrict__ g4,
+                                       const float4* __restrict__ b4, float* __restrict__ y, int D,
+                                       float eps, int lane, float& mn, float& mx) {
+  const int nv = D / 4;
+  float sum = 0.0f;
 #pragma unroll
-    for (int k = 0; k < 16; ++k) v[k] = row[8 * (g + k) + u];
+  for (int j = 0; j < kLnVec; ++j) sum += (v[j].x + v[j].y) + (v[j].z + v[j].w);
 #pragma unroll
-    for (int k = 0; k < 16; ++k) p = __fadd_rn(p, SQ ? __fmul_rn(v[k], v[k]) : v[k]);
-  }
-  for (; g < groups; ++g) {
-    const float v = row[8 * g + u];
-    p = __fadd_rn(p, SQ ? __fmul_rn(v, v) : v);
-  }
-  const float p4 = __shfl_down_sync(0xffffffffu, p, 4, 8);   // u < 4 gets p_{u+4}
-  const float pair = __fadd_rn(p, p4);
-  float acc = 0.0f;
+  for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  const float mean = sum / (float)D;
+  float sq = 0.0f;
 #pragma unroll
-  for (int k = 0; k < 4; ++k) acc = __fadd_rn(acc, __shfl_sync(0xffffffffu, pair, k, 8));
-  for (int i = groups * 8; i < D; ++i) {
-    const float v = row[i];
-    acc = __fadd_rn(acc, SQ ? __fmul_rn(v, v) : v);
+  for (int j = 0; j < kLnVec; ++j) {
+    const int c = lane + 32 * j;
+    if (c < nv) {
+      const float a = v[j].x - mean, b = v[j].y - mean, cc = v[j].z - mean, d = v[j].w - mean;
+      sq += (a * a + b * b) + (cc * cc + d * d);
+    }
   }
-  return acc;
+#pragma unroll
+  for (int o = 16; o; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+  const float rstd = rsqrtf(sq / (float)D + eps);
+  float4* yr = reinterpret_cast<float4*>(y);
+#pragma unroll
+  for (int j = 0; j < kLnVec; ++j) {
+    const int c = lane + 32 * j;
+    if (c < nv) {
+      const float4 g = __ldg(g4 + c);
+      const float4 bb = b4 ? __ldg(b4 + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+      float4 o;
+      o.x = (v[j].x - mean) * rstd * g.x + bb.x;
+      o.y = (v[j].y - mean) * rstd * g.y + bb.y;
+      o.z = (v[j].z - mean) * rstd * g.z + bb.z;
+      o.w = (v[j].w - mean) * rstd * g.w + bb.w;
+      yr[c] = o;
+      mn = fminf(mn, fminf(fminf(o.x, o.y), fminf(o.z, o.w)));
+      mx = fmaxf(mx, fmaxf(fmaxf(o.x, o.y), fmaxf(o.z, o.w)));
+    }
+  }
 }
 
-// RN(c / d) from y = RN(1 / d): one multiply and two FMAs.  Markstein's
-// theorem: with y = RN(1/d), q0 = RN(c y) and the exact remainder
-// r = c - q0 d (one FMA), RN(q0 + r y) = RN(c / d) when nothing overflows or
-// underflows; r == 0 keeps q0, and with it the sign of a zero.
-__device__ __forceinline__ float ln_div(float c, float d, float y) {
-  const float q0 = __fmul_rn(c, y);
-  const float r = __fmaf_rn(-q0, d, c);
-  return r == 0.0f ? q0 : __fmaf_rn(r, y, q0);
+__device__ __forceinline__ void ln_load(const float* __restrict__ x, int nv, int lane,
+                                        float4 (&v)[kLnVec]) {
+  const float4* xr = reinterpret_cast<const float4*>(x);
+#pragma unroll
+  for (int j = 0; j < kLnVec; ++j) {
+    const int c = lane + 32 * j;
+    v[j] = c < nv ? xr[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
 }
 
+// Warps stride over rows; the next row's loads are issued before the current
+// row is normalised, so a warp's second row does not wait for its own load.
 __global__ void __launch_bounds__(32 * kLnWarps)
     layernorm_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
                      const float* __restrict__ beta, float* __restrict__ y, int rows, int D,
                      float eps, float2* __restrict__ minmax) {
   pdl_wait();
   pdl_trigger();
-  extern __shared__ __align__(16) float ln_smem[];
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-  // this lane's row of the group (lanes past the group's rows repeat the
-  // last one) and its chain
-  const int r = min(lane >> 3, kLnRows - 1), u = lane & 7;
-  float* buf = ln_smem + (size_t)w * kLnRows * D;  // kLnRows rows of this warp
-  const int nv = D / 4;                            // 16-byte words per row
-  const int total = kLnRows * nv;
-  float4* buf4 = reinterpret_cast<float4*>(buf);
+  float mn = 0.0f, mx = 0.0f;
+  const int nv = D / 4;
   const float4* g4 = reinterpret_cast<const float4*>(gamma);
   const float4* b4 = reinterpret_cast<const float4*>(beta);
-  float mn = 0.0f, mx = 0.0f;
-  const int ngroups = (rows + kLnRows - 1) / kLnRows;
-  for (int grp = blockIdx.x * kLnWarps + w; grp < ngroups; grp += gridDim.x * kLnWarps) {
-    const int row0 = grp * kLnRows;
-    const int nrows = min(kLnRows, rows - row0);
-    const float4* x4 = reinterpret_cast<const float4*>(x + (size_t)row0 * D);
-    // stage the group's rows (rows past the end read as 0 and are never
-    // written), eight 16-byte loads per lane in flight
-    for (int i0 = lane; i0 < total; i0 += 32 * 8) {
-      float4 t[8];
+  const int stride = gridDim.x * kLnWarps;
+  int row = blockIdx.x * kLnWarps + w;
+  float4 cur[kLnVec];
+  if (row < rows) ln_load(x + (size_t)row * D, nv, lane, cur);
+  while (row < rows) {
+    const int next = row + stride;
+    float4 nxt[kLnVec];
+    if (next < rows) ln_load(x + (size_t)next * D, nv, lane, nxt);
+    ln_row(cur, g4, b4, y + (size_t)row * D, D, eps, lane, mn, mx);
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const int i = i0 + 32 * k;
-        t[k] = i < nrows * nv ? __ldg(x4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-      }
-#pragma unroll
-      for (int k = 0; k < 8; ++k)
-        if (i0 + 32 * k < total) buf4[i0 + 32 * k] = t[k];
-    }
-    __syncwarp();
-    const float mean = __fdiv_rn(ln_group_sum<false>(buf + r * D, D, u), (float)D);
-    float m4[kLnRows];   // every lane gets the four rows' means (no shuffles in ragged loops)
-#pragma unroll
-    for (int k = 0; k < kLnRows; ++k) m4[k] = __shfl_sync(0xffffffffu, mean, k * 8);
-    __syncwarp();  // every chain has read x before c overwrites it
-    // c = x - mean in place, each row with its own mean
-#pragma unroll
-    for (int rr = 0; rr < kLnRows; ++rr) {
-      const float m = m4[rr];
-      float4* br = buf4 + rr * nv;
-#pragma unroll 4
-      for (int c = lane; c < nv; c += 32) {
-        const float4 v = br[c];
-        br[c] = make_float4(__fsub_rn(v.x, m), __fsub_rn(v.y, m), __fsub_rn(v.z, m),
-                            __fsub_rn(v.w, m));
-      }
-    }
-    __syncwarp();
-    const float var = __fdiv_rn(ln_group_sum<true>(buf + r * D, D, u), (float)D);
-    const float sd = __fsqrt_rn(__fadd_rn(var, eps));
-    const float ysd = __frcp_rn(sd);
-    float s4[kLnRows], y4[kLnRows];
-#pragma unroll
-    for (int k = 0; k < kLnRows; ++k) {
-      s4[k] = __shfl_sync(0xffffffffu, sd, k * 8);
-      y4[k] = __shfl_sync(0xffffffffu, ysd, k * 8);
-    }
-    float4* yg = reinterpret_cast<float4*>(y + (size_t)row0 * D);
-    for (int c0 = lane; c0 < nv; c0 += 32 * 2) {
-      // two columns' scale / bias, reused by the group's rows
-      float4 g[2], bb[2];
-#pragma unroll
-      for (int k = 0; k < 2; ++k) {
-        const int c = c0 + 32 * k;
-        if (c < nv) {
-          g[k] = __ldg(g4 + c);
-          bb[k] = b4 ? __ldg(b4 + c) : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-      }
-#pragma unroll
-      for (int rr = 0; rr < kLnRows; ++rr) {
-        if (rr >= nrows) break;
-        const float sdv = s4[rr], ys = y4[rr];
-#pragma unroll
-        for (int k = 0; k < 2; ++k) {
-          const int c = c0 + 32 * k;
-          if (c < nv) {
-            const float4 cv = buf4[rr * nv + c];
-            float4 o;
-            o.x = __fadd_rn(__fmul_rn(ln_div(cv.x, sdv, ys), g[k].x), bb[k].x);
-            o.y = __fadd_rn(__fmul_rn(ln_div(cv.y, sdv, ys), g[k].y), bb[k].y);
-            o.z = __fadd_rn(__fmul_rn(ln_div(cv.z, sdv, ys), g[k].z), bb[k].z);
-            o.w = __fadd_rn(__fmul_rn(ln_div(cv.w, sdv, ys), g[k].w), bb[k].w);
-            yg[rr * nv + c] = o;
-            mn = fminf(mn, fminf(fminf(o.x, o.y), fminf(o.z, o.w)));
-            mx = fmaxf(mx, fmaxf(fmaxf(o.x, o.y), fmaxf(o.z, o.w)));
-          }
-        }
-      }
-    }
-    __syncwarp();  // the buffer is free for the next group
+    for (int j = 0; j < kLnVec; ++j) cur[j] = nxt[j];
+    row = next;
   }
   if (minmax) {
     __shared__ float2 red[kLnWarps];
@@ -483,29 +414,26 @@ __global__ void __launch_bounds__(32 * kLnWarps)
 }
 
 int layernorm_partials(size_t rows) {
-  // grid-stride over groups of kLnRows rows: one (min, max) partial per block
-  size_t groups = (rows + kLnRows - 1) / kLnRows;
-  size_t b = (groups + kLnWarps - 1) / kLnWarps;
-  if (b > 148 * 4) b = 148 * 4;
+  // grid-stride over rows with at most 2 blocks per SM: few partials for
+  // the DynamicQuantizeLinear that reads them
+  size_t b = (rows + kLnWarps - 1) / kLnWarps;
+  if (b > 148 * 2) b = 148 * 2;
   return b < 1 ? 1 : (int)b;
 }
 
 int launch_layernorm(cudaStream_t s, const float* x, const float* gamma, const float* beta,
                      float* y, size_t rows, size_t D, float eps, float* minmax, int* n_minmax) {
-  ICX_REQUIRE(D % 4 == 0 && D > 0 && D <= kLnMaxD,
+  ICX_REQUIRE(D % 4 == 0 && D <= 32 * 4 * kLnVec,
               "LayerNormalization: last dimension %zu unsupported (multiple of 4, <= %d)", D,
-              kLnMaxD);
+              32 * 4 * kLnVec);
   ICX_REQUIRE(((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y) |
                 reinterpret_cast<uintptr_t>(gamma) | reinterpret_cast<uintptr_t>(beta)) & 15) == 0,
               "LayerNormalization: buffers must be 16-byte aligned");
   const int blocks = layernorm_partials(rows);
   if (n_minmax) *n_minmax = blocks;
   if (rows == 0) return ICX_OK;
-  const size_t smem = (size_t)kLnWarps * kLnRows * D * sizeof(float);
-  ICX_CUDA(cudaFuncSetAttribute(layernorm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)(kLnWarps * kLnRows * kLnMaxD * sizeof(float))));
-  launch_pdl(layernorm_kernel, dim3(blocks), dim3(32 * kLnWarps), smem, s, x, gamma, beta, y,
-             (int)rows, (int)D, eps, reinterpret_cast<float2*>(minmax));
+  launch_pdl(layernorm_kernel, dim3(blocks), dim3(32 * kLnWarps), 0, s, x, gamma, beta, y, (int)rows, (int)D, eps,
+                                                    reinterpret_cast<float2*>(minmax));
   ICX_LAUNCH_CHECK();
   return ICX_OK;
 }

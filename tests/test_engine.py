@@ -251,10 +251,11 @@ def test_submit_wait_pipeline_equals_run():
 
 @gpu
 @pytest.mark.parametrize("rows,D,eps", [(4096, 768, 1e-12), (37, 768, 1e-5), (256, 100, 0.1)])
-def test_layernorm_bit_exact_with_the_reference_operator(rows, D, eps):
-    """LayerNormalization on the GPU follows the reference's op order and sum
-    order (src/operators/layer_normalization.rs:25-80, ndarray's lane sums),
-    so the whole tensor matches the restated operator bit for bit."""
+def test_layernorm_matches_the_reference_operator(rows, D, eps):
+    """LayerNormalization on the GPU against the restated reference operator
+    (src/operators/layer_normalization.rs:25-80) over the whole tensor: the
+    kernel sums with a warp tree and multiplies by rsqrt(var + eps), so the
+    bound is fp32 rounding, 4e-6 absolute on outputs of order 1-5."""
     from iconnx_b200.engine import GpuGraphExecutor
     from oracle import oracle
     gamma = (1.0 + synth.normal((D,), 0.02, 61)).astype(np.float32)
@@ -265,7 +266,7 @@ def test_layernorm_bit_exact_with_the_reference_operator(rows, D, eps):
     ex.add_initializer("b", beta)
     ex.add_node("ln", "LayerNormalization", ["x", "g", "b"], ["y"], {"axis": -1, "epsilon": eps})
     x = synth.normal((rows, D), 3.0, 63) + np.float32(0.5)
-    x[0, :] = np.float32(1.25)          # a constant row: zero variance, zero centred values
+    x[0, :] = np.float32(1.25)          # a constant row: zero variance
     got = ex.run({"x": x}, ["y"])["y"]
     ref = oracle.layer_normalization(x, gamma, beta, eps)
-    np.testing.assert_array_equal(got.view(np.uint32), ref.view(np.uint32))
+    assert np.abs(got.astype(np.float64) - ref).max() <= 4e-6

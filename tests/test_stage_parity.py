@@ -3,8 +3,7 @@ the benchmark configurations (the plans bench.py times: QKV merged, residual
 Adds fused, producer-fused (min, max) with quantise-only DynamicQuantizeLinear,
 CUDA-graph replay), against the oracle restatement of the reference operators.
 
-LayerNormalization steps are bit-exact too (the kernel follows the
-reference's op order and sum order).
+LayerNormalization steps are checked within 4e-6 (fp32 rounding order).
 
 Reference paths: GraphExecutor::run (src/graph_executor.rs:92-278) and
 GpuGraphExecutor::run (src/cuda/inference/mod.rs:428-464).  Each int8 stage
