@@ -52,8 +52,8 @@ INT8_PEAK_TOPS = 4500.0  # B200 dense int8, datasheet (no measured int8 peak on 
 # profiling size rule: its value is the M=8192 capture of
 # `bench.py --kernel gemm --shape 8192,4096,4096` scaled by the 8x rows, which
 # is how its traffic grows (A and the output scale with M).
-TRAFFIC_FFN1_M4096 = 5.575168e6 + 0.987904e6
-TRAFFIC_SWEEP_FROM_M8192 = 8 * (50.599424e6 + 81.093632e6)
+TRAFFIC_FFN1_M4096 = 5.869056e6 + 1.025024e6
+TRAFFIC_SWEEP_FROM_M8192 = 8 * (52.330496e6 + 83.63136e6)
 
 
 def roofline_traffic(kdesc: str):
