@@ -159,29 +159,34 @@ __device__ __forceinline__ uint32_t quant1(float xv, const DqlParams& p) {
 }
 
 // Four elements at once.  Common case (finite scale, no element within 1e-4
-// of a half-integer): rintf of x * (1/scale) + zp (one FMA), clamp to
-// [0, 255] with fminf/fmaxf (NaN -> 0), and read the integer out of the float's low byte
-// after adding 2^23; byte_perm packs the four bytes.  Otherwise every
-// element takes quant1 (with its exact f64 path where needed).
+// of a half-integer): u = x * (1/scale) + zp in one FMA, clamped to [0, 255]
+// with fmaxf / fminf (NaN -> 0; clamping first is exact because the bounds
+// are integers), then rounded to nearest even by adding 1.5 * 2^23: the sum
+// lies in [2^23, 2^24), where the float spacing is 1, so its low byte is the
+// quantised value and subtracting the constant again gives it as a float.
+// All full-rate FP32 operations; one compare per four elements decides
+// whether any of them lies in the near-tie band.  Otherwise every element
+// takes quant1 (with its exact f64 path where needed).
 template <bool SUM>
 __device__ __forceinline__ uint32_t quant4(float4 v, const DqlParams& p, uint32_t& sum) {
   if (p.fast) {
     // u = x * f32(1/scale) + zp in one rounding: |u - (x/scale + zp)| <=
     // 255 * 2^-24 + 2^-15 < 4.6e-5 (|u| < 512), so away from the 1e-4 band
     // around half-integers rint(u) = rte(x/scale) + zp (zp is an integer)
-    const float u0 = __fmaf_rn(v.x, p.inv32, p.zpf), u1 = __fmaf_rn(v.y, p.inv32, p.zpf);
-    const float u2 = __fmaf_rn(v.z, p.inv32, p.zpf), u3 = __fmaf_rn(v.w, p.inv32, p.zpf);
-    const float r0 = rintf(u0), r1 = rintf(u1), r2 = rintf(u2), r3 = rintf(u3);
-    const bool near = (fabsf(fabsf(u0 - r0) - 0.5f) <= 1e-4f) | (fabsf(fabsf(u1 - r1) - 0.5f) <= 1e-4f) |
-                      (fabsf(fabsf(u2 - r2) - 0.5f) <= 1e-4f) | (fabsf(fabsf(u3 - r3) - 0.5f) <= 1e-4f);
-    if (!near) {
-      const float q0 = fminf(fmaxf(r0, 0.0f), 255.0f);
-      const float q1 = fminf(fmaxf(r1, 0.0f), 255.0f);
-      const float q2 = fminf(fmaxf(r2, 0.0f), 255.0f);
-      const float q3 = fminf(fmaxf(r3, 0.0f), 255.0f);
+    constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+    const float c0 = fminf(fmaxf(__fmaf_rn(v.x, p.inv32, p.zpf), 0.0f), 255.0f);
+    const float c1 = fminf(fmaxf(__fmaf_rn(v.y, p.inv32, p.zpf), 0.0f), 255.0f);
+    const float c2 = fminf(fmaxf(__fmaf_rn(v.z, p.inv32, p.zpf), 0.0f), 255.0f);
+    const float c3 = fminf(fmaxf(__fmaf_rn(v.w, p.inv32, p.zpf), 0.0f), 255.0f);
+    const float t0 = __fadd_rn(c0, kRound), t1 = __fadd_rn(c1, kRound);
+    const float t2 = __fadd_rn(c2, kRound), t3 = __fadd_rn(c3, kRound);
+    const float q0 = __fsub_rn(t0, kRound), q1 = __fsub_rn(t1, kRound);
+    const float q2 = __fsub_rn(t2, kRound), q3 = __fsub_rn(t3, kRound);
+    const float d = fmaxf(fmaxf(fabsf(c0 - q0), fabsf(c1 - q1)), fmaxf(fabsf(c2 - q2), fabsf(c3 - q3)));
+    if (d < 0.5f - 1e-4f) {
       if (SUM) sum += (uint32_t)((q0 + q1) + (q2 + q3));
-      const uint32_t b0 = __float_as_uint(q0 + 8388608.0f), b1 = __float_as_uint(q1 + 8388608.0f);
-      const uint32_t b2 = __float_as_uint(q2 + 8388608.0f), b3 = __float_as_uint(q3 + 8388608.0f);
+      const uint32_t b0 = __float_as_uint(t0), b1 = __float_as_uint(t1);
+      const uint32_t b2 = __float_as_uint(t2), b3 = __float_as_uint(t3);
       return __byte_perm(__byte_perm(b0, b1, 0x0040), __byte_perm(b2, b3, 0x0040), 0x5410);
     }
   }
