@@ -34,6 +34,8 @@ PROTOTYPES = {
                                          _vp, _vp]),
     "icx_quant_linear": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _sz, _sz, _vp, _i, _vp, _i,
                               _vp, _i, _vp, _vp, _vp, _vp]),
+    "icx_quant_linear_layernorm": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _sz, _sz, _vp, _i,
+                                        _vp, _i, _vp, _vp, _vp, _vp, ctypes.c_float, _vp, _vp, _vp]),
     "icx_dql_f32_u8_noalloc": (_i, [_vp, _vp, _sz, _vp, _vp, _vp, _vp, _sz]),
     "icx_dql_quantize_f32_u8": (_i, [_vp, _vp, _sz, _vp, _i, _vp, _vp, _vp, _vp, _sz]),
     "icx_dequantize_linear": (_i, [_vp, _vp, _i, _sz, _sz, _sz, _vp, _sz, _vp, _vp]),

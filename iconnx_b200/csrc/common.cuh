@@ -326,6 +326,16 @@ __device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_
       : "memory");
 }
 
+// Stores 32 consecutive columns of this warp's 32 lanes (one register each)
+// as two 16-column stores.
+__device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
+  const uint32_t (&lo)[16] = *reinterpret_cast<const uint32_t(*)[16]>(&r[0]);
+  const uint32_t (&hi)[16] = *reinterpret_cast<const uint32_t(*)[16]>(&r[16]);
+  tmem_st_32x32b_x16(taddr, lo);
+  tmem_st_32x32b_x16(taddr + 16, hi);
+}
+
+
 __device__ __forceinline__ void tmem_st_wait() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
@@ -385,6 +395,48 @@ __device__ __forceinline__ uint32_t cluster_addr(const void* local, uint32_t ran
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr(local)), "r"(rank));
   return r;
 }
+__device__ __forceinline__ void fence_acq_rel_cluster() {
+  asm volatile("fence.acq_rel.cluster;" ::: "memory");
+}
+
+// Store a float into shared memory at a shared::cluster address (this
+// CTA's or another CTA's of the cluster).
+__device__ __forceinline__ void st_cluster_f32(uint32_t addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+
+// Store two floats (8-byte aligned) at a shared::cluster address.
+__device__ __forceinline__ void st_cluster_f32x2(uint32_t addr, float a, float b) {
+  asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(addr), "f"(a), "f"(b) : "memory");
+}
+
+// Bounded wait on a local mbarrier whose arrivals come from other CTAs of
+// the cluster (release.cluster): acquires at cluster scope, so their
+// stores before the arrival are visible after it.
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, int code) {
+  auto try_wait = [&]() {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+  };
+  if (try_wait()) return true;
+  const uint64_t t0 = globaltimer_ns();
+  uint32_t n = 0;
+  while (!try_wait()) {
+    if ((++n & 63) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
+      record_status(code);
+      return false;
+    }
+  }
+  return true;
+}
+
 // Arrive on an mbarrier given by its shared::cluster address (this CTA's or
 // the peer's), releasing this thread's prior memory accesses cluster-wide.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar) {

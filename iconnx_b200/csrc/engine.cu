@@ -148,6 +148,10 @@ struct Val {
 struct FusedQL {
   std::string q, s, z, w, ws, bz, bias, residual, out;
   bool gelu = false;
+  // LayerNormalization of the residual sum, in the same kernel (out is then
+  // the LayerNorm's output)
+  std::string ln_gamma, ln_beta;
+  float ln_eps = 0.0f;
   std::vector<FusedQL> parts;  // non-empty: several Linears merged along N
 };
 
@@ -160,6 +164,17 @@ struct FusedAttn {
   int64_t B = 0, S = 0, H = 0, nh = 0, dh = 0;
   bool mask_per_batch = true;
 };
+
+// QuantLinear + residual + LayerNorm in one kernel (default on);
+// ICONNX_LN_FUSE=0 keeps the LayerNorm a step of its own (read once, for
+// measurement).
+static bool ln_fuse_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("ICONNX_LN_FUSE");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
 
 struct Step {
   std::string node, op, out;
@@ -1144,6 +1159,28 @@ class Engine {
           }
         }
       }
+      // [LayerNormalization] of the residual sum over its last axis, done by
+      // a cluster of the GEMM's CTAs that together hold whole rows
+      if (!f.residual.empty() && ln_fuse_enabled() && sole_consumer(cur) >= 0 && !is_requested(cur)) {
+        const int ln = sole_consumer(cur);
+        const NodeDef& L = nodes_[ln];
+        const Init* g = L.op == "LayerNormalization" && L.in.size() >= 2 ? init_of(L.in[1]) : nullptr;
+        const Init* b = L.in.size() > 2 && !L.in[2].empty() ? init_of(L.in[2]) : nullptr;
+        const int64_t axis = L.op == "LayerNormalization" ? L.geti("axis", -1) : 0;
+        const int64_t rank = (int64_t)vals_[cur].shape.size();
+        bool only_y = true;
+        for (size_t k = 1; k < L.out.size(); ++k) only_y = only_y && L.out[k].empty();
+        if (g && L.in[0] == cur && g->dtype == ICX_F32 && numel(g->shape) == N &&
+            (L.in.size() <= 2 || L.in[2].empty() || (b && b->dtype == ICX_F32 && numel(b->shape) == N)) &&
+            (axis == -1 || axis == rank - 1) && only_y &&
+            quant_linear_ln_supported((size_t)w->shape[0], (size_t)N)) {
+          f.ln_gamma = L.in[1];
+          f.ln_beta = L.in.size() > 2 ? L.in[2] : std::string();
+          f.ln_eps = L.getf("epsilon", 1e-5f);
+          chain.push_back(ln);
+          cur = L.out[0];
+        }
+      }
       f.out = cur;
       for (int c : chain) skip_.insert(c);
       // the scale product is computed inside the kernel when nothing else reads it
@@ -1603,14 +1640,27 @@ class Engine {
     const float* bp = merged ? p.bias : (bias ? static_cast<const float*>(bias->dev) : nullptr);
     Prepared pw = p;
     const float* res = f.residual.empty() ? nullptr : static_cast<const float*>(resolve(f.residual));
+    const bool ln = !f.ln_gamma.empty();
     const std::string label = gelu ? "QuantLinear+GELU"
+                              : ln ? "QuantLinear+Residual+LayerNorm"
                               : res ? "QuantLinear+Residual"
                               : merged ? "QuantLinear(QKV)" : "QuantLinear";
-    add_step(n, label, f.out, [=](cudaStream_t s) {
-      return icx_quant_linear(s, qp, sp, zp, rows, static_cast<const int8_t*>(pw.bt), pw.colsum,
-                              (size_t)M, (size_t)K, (size_t)pw.N, wsp, ws_pc, bzp, bz_pc, bp,
-                              gelu ? 1 : 0, res, out, mm, mmc);
-    }, 1);
+    if (ln) {
+      const float* gp = static_cast<const float*>(init_of(f.ln_gamma)->dev);
+      const float* bp2 = f.ln_beta.empty() ? nullptr : static_cast<const float*>(init_of(f.ln_beta)->dev);
+      const float eps = f.ln_eps;
+      add_step(n, label, f.out, [=](cudaStream_t s) {
+        return icx_quant_linear_layernorm(s, qp, sp, zp, rows, static_cast<const int8_t*>(pw.bt),
+                                          pw.colsum, (size_t)M, (size_t)K, (size_t)pw.N, wsp, ws_pc,
+                                          bzp, bz_pc, bp, res, gp, bp2, eps, out, mm, mmc);
+      }, 1);
+    } else {
+      add_step(n, label, f.out, [=](cudaStream_t s) {
+        return icx_quant_linear(s, qp, sp, zp, rows, static_cast<const int8_t*>(pw.bt), pw.colsum,
+                                (size_t)M, (size_t)K, (size_t)pw.N, wsp, ws_pc, bzp, bz_pc, bp,
+                                gelu ? 1 : 0, res, out, mm, mmc);
+      }, 1);
+    }
     // the weights of the step by their initializer names (merged: one
     // '|'-separated entry per part, in column order)
     std::string w, wsn, bzn, bn;
@@ -1626,6 +1676,11 @@ class Engine {
     steps_.back().info = "q=" + f.q + ";s=" + f.s + ";z=" + f.z + ";w=" + w + ";ws=" + wsn +
                          ";bz=" + bzn + ";bias=" + bn + ";residual=" + f.residual +
                          ";gelu=" + (gelu ? "1" : "0") + ";out=" + f.out;
+    if (ln) {
+      char eb[32];
+      snprintf(eb, sizeof(eb), "%.9g", (double)f.ln_eps);
+      steps_.back().info += ";ln_gamma=" + f.ln_gamma + ";ln_beta=" + f.ln_beta + ";ln_eps=" + eb;
+    }
     return ICX_OK;
   }
 

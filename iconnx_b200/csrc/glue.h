@@ -21,6 +21,10 @@ int launch_binary(cudaStream_t s, int op, const float* a, const std::vector<int6
                   const float* b, const std::vector<int64_t>& bshape, float* out,
                   const std::vector<int64_t>& oshape);
 int layernorm_partials(size_t rows);
+// Whether icx_quant_linear_layernorm runs for this K and N on the current
+// device (qgemm.cu).
+bool quant_linear_ln_supported(size_t K, size_t N);
+
 int launch_layernorm(cudaStream_t s, const float* x, const float* gamma, const float* beta,
                      float* y, size_t rows, size_t D, float eps, float* minmax, int* n_minmax);
 int launch_scale_mask_softmax(cudaStream_t s, const float* x, float* y, size_t rows, size_t D,

@@ -43,7 +43,10 @@ constexpr int kBM = 128;      // rows per tile (UMMA M)
 constexpr int kBK = 128;      // K bytes per stage (one 128-byte swizzle atom)
 constexpr int kUmmaK = 32;    // K per tcgen05.mma kind::i8
 
-enum EpiMode { kEpiS32 = 0, kEpiF32 = 1, kEpiGelu = 2 };
+// kEpiLn: dequantisation, bias, residual Add and the LayerNormalization of
+// the whole row, computed by a cluster of CTAs that together hold the row
+// (ln_epilogue below).
+enum EpiMode { kEpiS32 = 0, kEpiF32 = 1, kEpiGelu = 2, kEpiLn = 3 };
 
 struct GemmArgs {
   int M, N, K;
@@ -62,6 +65,9 @@ struct GemmArgs {
   const float* residual;  // nullable: f32 [M, N] added after the bias (residual Add)
   float2* minmax;         // nullable: per-CTA (min, max) of the f32 output,
                           // seeded with 0 like DynamicQuantizeLinear's scan
+  const float* ln_gamma;  // kEpiLn: LayerNormalization scale [N]
+  const float* ln_beta;   // kEpiLn: nullable, bias [N]
+  float ln_eps;
 };
 
 __device__ __forceinline__ int32_t ld_zp(const void* p, int is_signed,
@@ -125,7 +131,7 @@ struct Cfg {
   static constexpr int kPairStages =
       (227 * 1024 - EW * kStageOutBytes - EW * kOpWarpBytes - kBarBytes - 1024) / kStageBytes;
   static constexpr int kStages = CG == 2 ? (kPairStages > 8 ? 8 : kPairStages)
-                                 : DEEP ? (BN == 256 ? 4 : BN == 192 ? 4 : 5)
+                                 : DEEP ? (BN == 256 ? 4 : BN == 192 ? (EW == 16 ? 3 : 4) : 5)
                                  : BN == 256 ? 3
                                  : BN == 192 ? (EW == 16 ? 3 : 4)
                                              : (EW == 16 ? 4 : 5);
@@ -290,6 +296,252 @@ __device__ __forceinline__ float4 ld4f(const float* p, int n, int N, bool vec) {
                      n + 3 < N ? p[n + 3] : 0.f);
 }
 
+// Epilogue of the LayerNorm-fused GEMM (kEpiLn): a cluster of N / BN CTAs
+// (2 to 4), CTA rank r of the cluster holding column tile r of the same 128
+// rows, so the cluster holds whole rows.  Epilogue warp e (EW = 12: three
+// warps per TMEM lane quadrant, 16-column chunks part, part + 3, ...) per
+// tile:
+//   1. turns its chunks' accumulators into z = (acc * scale + bias) +
+//      residual exactly as the QuantLinear epilogue does (the residual of
+//      the next chunk in flight meanwhile) and writes z back over the
+//      accumulator columns in TMEM; it also sums z - k0 and (z - k0)^2 with
+//      k0 the thread's first value;
+//   2. row statistics in one exchange: each thread's (sum, M2) of its 64
+//      values (M2 about their own mean, from the shifted sums) goes to every
+//      CTA of the cluster (st.shared::cluster into slot [rank][part][row]; a
+//      cluster-scope fence per lane and one release.cluster arrive per warp
+//      on each CTA's barrier); after the wait each thread combines the
+//      3 * (N / BN) pairs of its row with Chan's parallel formula, M2 = sum
+//      M2_i + sum n_i (mean_i - mean)^2, var = M2 / N, rstd = rsqrt(var +
+//      eps);
+//   3. y = (z - mean) * rstd * gamma + beta, the (min, max) of y for the
+//      DynamicQuantizeLinear that reads it; each 32 x 16 block goes through
+//      a swizzled shared-memory tile so that four lanes store one row's 64
+//      contiguous bytes; then the accumulator goes back to the MMA warp.
+// The exchange buffers and barriers alternate by tile parity: a CTA writes a
+// buffer again only after every CTA arrived for the tile in between, which
+// each does after reading that buffer.
+// Semantics: the reference's LayerNormalization (layer_normalization.rs:
+// 25-80) of the Add output, two-pass mean / variance there and the stable
+// parallel combination here (fp32 rounding, as the LayerNorm kernel).
+template <int BN, bool HAS_BZ, bool HAS_BIAS, int EW>
+__device__ __forceinline__ void ln_epilogue(const GemmArgs& args, uint32_t tmem_base, uint64_t* tfull,
+                                            uint64_t* tempty, uint64_t* lnbar, float* xbuf,
+                                            uint8_t* ops, float2* red, int warp, int lane, int tile0,
+                                            int tstep, int ntiles, int num_n) {
+  constexpr int kParts = EW / 4;
+  constexpr int kCW = 16;                           // chunk width (columns)
+  static_assert(BN % (kCW * kParts) == 0, "LayerNorm epilogue: whole chunks per warp");
+  constexpr int kPerWarp = BN / kCW / kParts;       // chunks per warp
+  constexpr float kNLocal = (float)(kPerWarp * kCW);
+  const int e = warp - 2, quad = warp & 3, part = e >> 2;
+  const int M = args.M, N = args.N, K = args.K;
+  const int ncl = num_n;                            // CTAs in the cluster
+  const uint32_t my_rank = cluster_ctarank();
+  const int row = quad * 32 + lane;
+  const uint32_t za = args.a_zp ? (uint32_t)ld_zp(args.a_zp, args.a_zp_signed, 0) : 0u;
+  const float a_scale = *args.a_scale;
+  const float sc_scalar = __fmul_rn(a_scale, args.w_scale[0]);
+  const bool sc_per_col = args.w_scale_per_col != 0;
+  const bool bz_per_col = args.b_zp_per_col != 0;
+  const int32_t bz_scalar = HAS_BZ ? ld_zp(args.b_zp, args.b_zp_signed, 0) : 0;
+  // The CTA's column tile is the same for every tile it runs (its rank in
+  // the cluster): its column operands go to shared memory once.
+  int32_t* op_cs = reinterpret_cast<int32_t*>(ops);
+  float* op_sc = reinterpret_cast<float*>(op_cs + BN);
+  float* op_bi = op_sc + BN;
+  int32_t* op_bz = reinterpret_cast<int32_t*>(op_bi + BN);
+  float* op_g = reinterpret_cast<float*>(op_bz + BN);
+  float* op_b = op_g + BN;
+  // exchange buffers: two (tile parity) of [kMaxCl][kParts][kBM] float2;
+  // then this warp's 32 x 16 transpose tile
+  constexpr int kMaxCl = 4;
+  float2* xch = reinterpret_cast<float2*>(xbuf);
+  float* tile_t = xbuf + 2 * 2 * kMaxCl * kParts * kBM + e * 32 * kCW;
+  {
+    const int ti = threadIdx.x - 64, n = (int)my_rank * BN + ti;
+    if (ti < BN) {
+      const bool nv = n < N;
+      op_cs[ti] = nv ? args.colsum[n] : 0;
+      op_sc[ti] = !nv ? 0.0f : sc_per_col ? __fmul_rn(a_scale, args.w_scale[n]) : sc_scalar;
+      op_bi[ti] = HAS_BIAS && nv ? args.bias[n] : 0.0f;
+      op_bz[ti] = HAS_BZ && bz_per_col && nv ? ld_zp(args.b_zp, args.b_zp_signed, n) : bz_scalar;
+      op_g[ti] = nv ? args.ln_gamma[n] : 0.0f;
+      op_b[ti] = args.ln_beta && nv ? args.ln_beta[n] : 0.0f;
+    }
+    epi_sync<EW>();
+  }
+  int acc = 0;
+  uint32_t acc_phase = 0;
+  int xb = 0;              // exchange buffer / barrier of this tile
+  uint32_t xphase = 0;     // parity of barrier xb's next phase
+  bool ok = true;
+  float run_mn = 0.0f, run_mx = 0.0f;
+  const int kXch = kMaxCl * kParts * kBM;            // float2 per exchange buffer
+  const int slot = ((int)my_rank * kParts + part) * kBM + row;
+  for (int t = tile0; t < ntiles; t += tstep) {
+    const int m0 = (t / num_n) * kBM, n0 = (t % num_n) * BN;
+    const int m = m0 + row;
+    const bool mv = m < M;
+    const float* res_row = args.residual + (size_t)(mv ? m : 0) * N + n0;
+    auto load_res = [&](int j, float (&rv)[kCW]) {
+      const float4* rr = reinterpret_cast<const float4*>(res_row + (part + kParts * j) * kCW);
+#pragma unroll
+      for (int q = 0; q < kCW / 4; ++q) {
+        const float4 r4 = mv ? __ldg(rr + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+        rv[4 * q] = r4.x;
+        rv[4 * q + 1] = r4.y;
+        rv[4 * q + 2] = r4.z;
+        rv[4 * q + 3] = r4.w;
+      }
+    };
+    // 1. the first chunk's residual values are in flight during the wait
+    float res[kCW];
+    load_res(0, res);
+    uint32_t kza_rs = 0;
+    if (HAS_BZ) kza_rs = (uint32_t)K * za - (mv ? (uint32_t)args.rowsum[m] : 0u);
+    if (ok) ok = mbar_wait_warp(&tfull[acc], acc_phase, ICX_DEVICE_TIMEOUT_EPILOGUE);
+    tc_fence_after();
+    const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
+    // sums of z - k0 and of its squares, k0 = this thread's first value (a
+    // shift that keeps the local variance well conditioned)
+    float k0 = 0.0f, s1 = 0.0f, s2 = 0.0f;
+#pragma unroll
+    for (int j = 0; j < kPerWarp; ++j) {
+      const int cl = (part + kParts * j) * kCW;   // first column of the chunk in the tile
+      uint32_t r[kCW];
+      if (ok) {
+        tmem_ld_32x32b_x16(t_row + (uint32_t)cl, r);
+        tmem_ld_wait_regs16(r);
+      }
+      float res_next[kCW];
+      if (j + 1 < kPerWarp) load_res(j + 1, res_next);
+#pragma unroll
+      for (int q = 0; q < kCW / 4; ++q) {
+        const int c4 = cl + 4 * q;
+        const int4 cs = *reinterpret_cast<const int4*>(op_cs + c4);
+        const float4 sc = *reinterpret_cast<const float4*>(op_sc + c4);
+        const float4 bi = *reinterpret_cast<const float4*>(op_bi + c4);
+        const int4 bz = *reinterpret_cast<const int4*>(op_bz + c4);
+        int32_t v0 = (int32_t)(r[4 * q + 0] - za * (uint32_t)cs.x);
+        int32_t v1 = (int32_t)(r[4 * q + 1] - za * (uint32_t)cs.y);
+        int32_t v2 = (int32_t)(r[4 * q + 2] - za * (uint32_t)cs.z);
+        int32_t v3 = (int32_t)(r[4 * q + 3] - za * (uint32_t)cs.w);
+        if (HAS_BZ) {
+          v0 = (int32_t)((uint32_t)v0 + kza_rs * (uint32_t)bz.x);
+          v1 = (int32_t)((uint32_t)v1 + kza_rs * (uint32_t)bz.y);
+          v2 = (int32_t)((uint32_t)v2 + kza_rs * (uint32_t)bz.z);
+          v3 = (int32_t)((uint32_t)v3 + kza_rs * (uint32_t)bz.w);
+        }
+        uint32_t o[4];
+        finish2<kEpiF32, HAS_BIAS>(v0, v1, sc.x, sc.y, bi.x, bi.y, o[0], o[1]);
+        finish2<kEpiF32, HAS_BIAS>(v2, v3, sc.z, sc.w, bi.z, bi.w, o[2], o[3]);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const float zv = __fadd_rn(__uint_as_float(o[u]), res[4 * q + u]);
+          if (j == 0 && q == 0 && u == 0) k0 = zv;
+          const float d = zv - k0;
+          s1 += d;
+          s2 = fmaf(d, d, s2);
+          r[4 * q + u] = __float_as_uint(zv);
+        }
+      }
+      // z back over its accumulator columns, read again to normalise
+      if (ok) tmem_st_32x32b_x16(t_row + (uint32_t)cl, r);
+      if (j + 1 < kPerWarp)
+#pragma unroll
+        for (int u = 0; u < kCW; ++u) res[u] = res_next[u];
+    }
+    tmem_st_wait();
+    // 2. the exchange: (sum, M2 about the local mean) of this thread's values
+    const float sum = fmaf(kNLocal, k0, s1);
+    const float m2 = fmaxf(s2 - s1 * (s1 / kNLocal), 0.0f);
+    float2* buf = xch + xb * kXch;
+    for (int r2 = 0; r2 < ncl; ++r2) st_cluster_f32x2(cluster_addr(buf + slot, (uint32_t)r2), sum, m2);
+    // every lane's stores are ordered cluster-wide before the warp's one
+    // arrival per CTA (lane r2 signals CTA r2, releasing at cluster scope)
+    fence_acq_rel_cluster();
+    __syncwarp();
+    if (lane < ncl) mbar_arrive_cluster(cluster_addr(&lnbar[xb], (uint32_t)lane));
+    if (ok) ok = mbar_wait_cluster(&lnbar[xb], xphase, ICX_DEVICE_TIMEOUT_EPILOGUE);
+    float mean, rstd;
+    {
+      float tot = 0.0f;
+      for (int i = 0; i < ncl * kParts; ++i) tot += buf[i * kBM + row].x;
+      mean = tot / (float)N;
+      float M2 = 0.0f;
+      for (int i = 0; i < ncl * kParts; ++i) {
+        const float2 p = buf[i * kBM + row];
+        const float d = p.x / kNLocal - mean;
+        M2 += fmaf(kNLocal * d, d, p.y);
+      }
+      rstd = rsqrtf(M2 / (float)N + args.ln_eps);
+    }
+    if (xb == 1) xphase ^= 1;
+    xb ^= 1;
+    // 3. normalise; each chunk through the transpose tile to row-contiguous
+    // stores (float4 p of row r at r * 16 + 4 * (p ^ ((r >> 1) & 3)): both
+    // the row-wise writes and the transposed reads are bank-conflict free)
+    float* out = static_cast<float*>(args.out);
+#pragma unroll
+    for (int j = 0; j < kPerWarp; ++j) {
+      const int cl = (part + kParts * j) * kCW;
+      uint32_t r[kCW];
+      if (ok) {
+        tmem_ld_32x32b_x16(t_row + (uint32_t)cl, r);
+        tmem_ld_wait_regs16(r);
+      }
+#pragma unroll
+      for (int q = 0; q < kCW / 4; ++q) {
+        const float4 g = *reinterpret_cast<const float4*>(op_g + cl + 4 * q);
+        const float4 b = *reinterpret_cast<const float4*>(op_b + cl + 4 * q);
+        float4 o;
+        o.x = (__uint_as_float(r[4 * q]) - mean) * rstd * g.x + b.x;
+        o.y = (__uint_as_float(r[4 * q + 1]) - mean) * rstd * g.y + b.y;
+        o.z = (__uint_as_float(r[4 * q + 2]) - mean) * rstd * g.z + b.z;
+        o.w = (__uint_as_float(r[4 * q + 3]) - mean) * rstd * g.w + b.w;
+        if (mv) {
+          run_mn = fminf(run_mn, fminf(fminf(o.x, o.y), fminf(o.z, o.w)));
+          run_mx = fmaxf(run_mx, fmaxf(fmaxf(o.x, o.y), fmaxf(o.z, o.w)));
+        }
+        *reinterpret_cast<float4*>(tile_t + lane * kCW + 4 * (q ^ ((lane >> 1) & 3))) = o;
+      }
+      __syncwarp();
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int rr = (lane >> 2) + 8 * i, c = lane & 3;
+        const float4 v = *reinterpret_cast<const float4*>(tile_t + rr * kCW + 4 * (c ^ ((rr >> 1) & 3)));
+        const int mr = m0 + quad * 32 + rr;
+        if (mr < M) *reinterpret_cast<float4*>(out + (size_t)mr * N + n0 + cl + 4 * c) = v;
+      }
+      __syncwarp();
+    }
+    // every column of the accumulator this warp owns has been read back
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&tempty[acc]);
+    acc ^= 1;
+    if (acc == 0) acc_phase ^= 1;
+  }
+  if (args.minmax != nullptr) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      run_mn = fminf(run_mn, __shfl_xor_sync(0xffffffffu, run_mn, o));
+      run_mx = fmaxf(run_mx, __shfl_xor_sync(0xffffffffu, run_mx, o));
+    }
+    if (lane == 0) red[e] = make_float2(run_mn, run_mx);
+    epi_sync<EW>();
+    if (e == 0 && lane == 0) {
+      float mn = 0.0f, mx = 0.0f;
+      for (int i = 0; i < EW; ++i) {
+        mn = fminf(mn, red[i].x);
+        mx = fmaxf(mx, red[i].y);
+      }
+      args.minmax[blockIdx.x] = make_float2(mn, mx);
+    }
+  }
+}
+
 template <int BN, int EPI, bool HAS_BZ, bool HAS_BIAS, bool DEEP, int EW, int CG>
 __global__ void __launch_bounds__(gemm_threads<EW>(), 1)
     qgemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA,
@@ -314,6 +566,8 @@ __global__ void __launch_bounds__(gemm_threads<EW>(), 1)
   float2* red = reinterpret_cast<float2*>(smem + C::kBarOffset + 256);
   // residual tile barriers, one per epilogue warp
   uint64_t* rbar = reinterpret_cast<uint64_t*>(smem + C::kBarOffset + 512);
+  // LayerNorm exchange barriers (kEpiLn), one per round
+  uint64_t* lnbar = reinterpret_cast<uint64_t*>(smem + C::kBarOffset + 768);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -337,6 +591,10 @@ __global__ void __launch_bounds__(gemm_threads<EW>(), 1)
       mbar_init(&tempty[a], CG * EW);   // the leader's counts both CTAs' epilogues
     }
     for (int w = 0; w < EW; ++w) mbar_init(&rbar[w], 1);
+    // LayerNorm exchange rounds: every epilogue warp of every CTA of the
+    // cluster arrives once per round
+    if (EPI == kEpiLn)
+      for (int r = 0; r < 2; ++r) mbar_init(&lnbar[r], (uint32_t)(num_n * EW));
     fence_barrier_init();
     fence_proxy_async_smem();
   }
@@ -356,9 +614,10 @@ __global__ void __launch_bounds__(gemm_threads<EW>(), 1)
     }
   }
   tc_fence_before();
-  // a pair's barriers are signalled across the pair: both CTAs' set-up must
-  // be visible before either starts
-  if (CG == 2) cluster_sync();
+  // a pair's barriers are signalled across the pair (and a LayerNorm
+  // cluster's across the cluster): every CTA's set-up must be visible before
+  // any starts
+  if (CG == 2 || EPI == kEpiLn) cluster_sync();
   else __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
@@ -455,6 +714,16 @@ __global__ void __launch_bounds__(gemm_threads<EW>(), 1)
         if (acc == 0) acc_phase ^= 1;
       }
     }
+  } else if constexpr (EPI == kEpiLn) {
+    static_assert(CG == 1, "LayerNorm epilogue: single-CTA tiles");
+    // the exchange buffers and the transpose tiles take the (unused) output
+    // staging area, the column operands the operand slices
+    static_assert(2 * 4 * (EW / 4) * kBM * 8 + EW * 32 * 16 * 4 <= C::kOutBufs * EW * kStageOutBytes,
+                  "exchange buffers");
+    static_assert(C::kStageOps && 6 * BN * 4 <= EW * C::kOpWarpBytes, "column operands");
+    ln_epilogue<BN, HAS_BZ, HAS_BIAS, EW>(args, tmem_base, tfull, tempty, lnbar,
+                                          reinterpret_cast<float*>(sOut), smem + C::kOpOffset, red,
+                                          warp, lane, tile0, tstep, ntiles, num_n);
   } else {
     // ----------------------------------------------------------- epilogue
     // Warp e owns TMEM lane quadrant (warp & 3) and the 32-column chunks
@@ -815,8 +1084,10 @@ __global__ void __launch_bounds__(gemm_threads<EW>(), 1)
   tc_fence_before();
   __syncwarp();
   // neither CTA of a pair leaves while the other may still signal its
-  // barriers or the leader's MMAs may still read its shared memory
-  if (CG == 2) cluster_sync();
+  // barriers or the leader's MMAs may still read its shared memory (nor a
+  // CTA of a LayerNorm cluster while the others may still write into its
+  // exchange buffers)
+  if (CG == 2 || EPI == kEpiLn) cluster_sync();
   else __syncthreads();
   if (warp == 1) {
     tc_fence_after();
@@ -951,7 +1222,7 @@ static int launch_tc(cudaStream_t s, const void* a, bool a_signed, const void* b
   rc = make_tmap(&tb, bt, (size_t)args.N, (size_t)args.K, BN / CG);
   if (rc) return rc;
   // TMA stores need a 16-byte aligned base and a row pitch multiple of 16 B
-  const int tma_store = C::kOutBufs > 0 && (args.N % 4 == 0) && aligned16(args.out);
+  const int tma_store = EPI != kEpiLn && C::kOutBufs > 0 && (args.N % 4 == 0) && aligned16(args.out);
   if (tma_store) {
     rc = make_out_tmap(&tout, args.out, (size_t)args.M, (size_t)args.N, EPI != kEpiS32);
     if (rc) return rc;
@@ -983,6 +1254,10 @@ static int launch_tc(cudaStream_t s, const void* a, bool a_signed, const void* b
   if (CG == 2)
     launch_pdl_cluster(kern, dim3(grid), dim3(gemm_threads<EW>()), C::kSmemBytes, s, 2u, ta, tb,
                        tout, tres, args, idesc, tma_store, vec_cols, tma_res);
+  else if (EPI == kEpiLn)
+    launch_pdl_cluster(kern, dim3(grid), dim3(gemm_threads<EW>()), C::kSmemBytes, s,
+                       (unsigned)(args.N / BN), ta, tb, tout, tres, args, idesc, tma_store, vec_cols,
+                       tma_res);
   else
     launch_pdl(kern, dim3(grid), dim3(gemm_threads<EW>()), C::kSmemBytes, s, ta, tb, tout, tres,
                args, idesc, tma_store, vec_cols, tma_res);
@@ -1302,6 +1577,103 @@ extern "C" int icx_quant_linear(void* stream, const uint8_t* d_q,
   cudaStream_t s = as_stream(stream);
   return gelu ? launch_gemm<kEpiGelu>(s, d_q, false, d_wt, true, g)
               : launch_gemm<kEpiF32>(s, d_q, false, d_wt, true, g);
+}
+
+// ------------------------------------------------ QuantLinear + LayerNorm
+// Epilogue warps of the LayerNorm-fused GEMM: three per TMEM lane quadrant,
+// four 16-column chunks each (64 values per thread within the 128
+// registers that 448 threads leave).
+constexpr int kLnWarps = 12;
+
+// Clusters of the LayerNorm-fused GEMM (N / 192 CTAs each) that can be
+// resident at once, per device, cluster size and ring depth (cached).
+template <bool DEEP>
+static int max_ln_clusters(int ncl) {
+  static int cached[64][9] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || ncl < 1 || ncl > 8) return 0;
+  if (cached[dev][ncl]) return cached[dev][ncl];
+  using C = Cfg<192, DEEP, kLnWarps, 1>;
+  auto kern = qgemm_tcgen05_kernel<192, kEpiLn, false, true, DEEP, kLnWarps, 1>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes) !=
+      cudaSuccess)
+    return 0;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(ncl * (148 / ncl));
+  cfg.blockDim = dim3(gemm_threads<kLnWarps>());
+  cfg.dynamicSmemBytes = C::kSmemBytes;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = ncl;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n < 1) {
+    cudaGetLastError();
+    return 0;
+  }
+  cached[dev][ncl] = n;
+  return n;
+}
+
+namespace icx {
+bool quant_linear_ln_supported(size_t K, size_t N);
+}  // namespace icx
+
+bool icx::quant_linear_ln_supported(size_t K, size_t N) {
+  if (K == 0 || K % 16 != 0 || K >= (1u << 30) || N % 192 != 0) return false;
+  const int ncl = (int)(N / 192);
+  if (ncl < 2 || ncl > 4) return false;
+  return (K >= 1536 ? max_ln_clusters<true>(ncl) : max_ln_clusters<false>(ncl)) > 0;
+}
+
+extern "C" int icx_quant_linear_layernorm(void* stream, const uint8_t* d_q, const float* d_a_scale,
+                                          const uint8_t* d_a_zp, const int32_t* d_rowsum_q,
+                                          const int8_t* d_wt, const int32_t* d_colsum, size_t M,
+                                          size_t K, size_t N, const float* d_w_scale,
+                                          int w_scale_per_col, const int8_t* d_b_zp, int b_zp_per_col,
+                                          const float* d_bias, const float* d_residual,
+                                          const float* d_gamma, const float* d_beta, float epsilon,
+                                          float* d_out, float* d_minmax, int* n_minmax) {
+  ICX_REQUIRE(M < (1u << 31), "QuantLinear+LayerNorm: shape too large");
+  ICX_REQUIRE(icx::quant_linear_ln_supported(K, N),
+              "QuantLinear+LayerNorm: K=%zu N=%zu unsupported (K %% 16 == 0, N = 192 x 2..4)", K, N);
+  if (n_minmax) *n_minmax = 0;
+  if (M == 0) return ICX_OK;
+  ICX_REQUIRE(d_q && d_wt && d_out && d_colsum && d_a_scale && d_w_scale && d_residual && d_gamma,
+              "QuantLinear+LayerNorm: null operand");
+  ICX_REQUIRE(d_b_zp == nullptr || d_rowsum_q != nullptr,
+              "QuantLinear+LayerNorm: b_zero_point needs the row sums of q");
+  ICX_REQUIRE(aligned16(d_q) && aligned16(d_wt) && aligned16(d_out) && aligned16(d_colsum) &&
+                  aligned16(d_residual) && aligned16(d_gamma) && (!d_beta || aligned16(d_beta)) &&
+                  (!d_bias || aligned16(d_bias)) && (!w_scale_per_col || aligned16(d_w_scale)) &&
+                  (!d_b_zp || !b_zp_per_col || (reinterpret_cast<uintptr_t>(d_b_zp) & 3) == 0),
+              "QuantLinear+LayerNorm: operands must be 16-byte aligned");
+  GemmArgs g{};
+  g.M = (int)M; g.N = (int)N; g.K = (int)K;
+  g.a_zp = d_a_zp; g.a_zp_signed = 0;
+  g.b_zp = d_b_zp; g.b_zp_signed = 1; g.b_zp_per_col = b_zp_per_col;
+  g.colsum = d_colsum; g.rowsum = d_rowsum_q;
+  g.a_scale = d_a_scale; g.w_scale = d_w_scale; g.w_scale_per_col = w_scale_per_col;
+  g.bias = d_bias;
+  g.residual = d_residual;
+  g.out = d_out;
+  g.minmax = reinterpret_cast<float2*>(d_minmax);
+  g.ln_gamma = d_gamma;
+  g.ln_beta = d_beta;
+  g.ln_eps = epsilon;
+  const int ncl = (int)(N / 192);
+  const bool deep = K >= 1536;
+  const long num_m = (long)((M + kBM - 1) / kBM);
+  const long cl = deep ? max_ln_clusters<true>(ncl) : max_ln_clusters<false>(ncl);
+  const int grid = (int)(num_m < cl ? num_m : cl) * ncl;
+  if (n_minmax) *n_minmax = grid;
+  cudaStream_t s = as_stream(stream);
+  return deep ? launch_tc<192, kEpiLn, true, kLnWarps, 1>(s, d_q, false, d_wt, true, g, grid)
+              : launch_tc<192, kEpiLn, false, kLnWarps, 1>(s, d_q, false, d_wt, true, g, grid);
 }
 
 extern "C" int icx_matmul_integer_rowsum(void* stream, const void* d_a, int a_type, size_t M,

@@ -214,6 +214,32 @@ def quant_linear(q: torch.Tensor, a_scale: torch.Tensor, a_zp: torch.Tensor, w: 
     return out
 
 
+def quant_linear_layernorm(q: torch.Tensor, a_scale: torch.Tensor, a_zp: torch.Tensor,
+                           w: PreparedWeight, w_scale: torch.Tensor, residual: torch.Tensor,
+                           gamma: torch.Tensor, beta: torch.Tensor | None = None,
+                           epsilon: float = 1e-5, bias: torch.Tensor | None = None,
+                           b_zp: torch.Tensor | None = None, rowsum: torch.Tensor | None = None,
+                           out: torch.Tensor | None = None,
+                           minmax: "MinMaxPartials | None" = None) -> torch.Tensor:
+    """LayerNormalization(QuantLinear(q) + residual) over the last axis in one
+    launch (N = 192 x 2..4); the residual sum itself is not written."""
+    K = q.shape[-1]
+    M = q.numel() // K
+    if K != w.K or w.dtype != torch.int8:
+        raise IcxError(-1, "QuantLinear+LayerNorm: weight must be Int8 with matching K")
+    if out is None:
+        out = torch.empty((*q.shape[:-1], w.N), dtype=torch.float32, device=q.device)
+    per_col_s = int(w_scale.numel() > 1)
+    per_col_z = int(b_zp is not None and b_zp.numel() > 1)
+    check(_lib.load().icx_quant_linear_layernorm(
+        _stream(q), _ptr(q), _ptr(a_scale), _ptr(a_zp), _ptr(rowsum), _ptr(w.bt), _ptr(w.colsum),
+        M, K, w.N, _ptr(w_scale), per_col_s, _ptr(b_zp), per_col_z, _ptr(bias), _ptr(residual),
+        _ptr(gamma), _ptr(beta), float(epsilon), _ptr(out),
+        None if minmax is None else minmax.buf.data_ptr(),
+        None if minmax is None else ctypes.byref(minmax.count)))
+    return out
+
+
 def gpu_dynamic_quantize_from_partials(x: torch.Tensor, minmax: MinMaxPartials,
                                        row_len: int | None = None):
     """DynamicQuantizeLinear whose min/max scan was done by x's producer."""

@@ -205,6 +205,29 @@ ICX_API int icx_quant_linear(void* stream, const uint8_t* d_q, const float* d_a_
                      int* n_minmax);
 
 /* ======================================================================== *
+ * QuantLinear + residual Add + LayerNormalization in one launch:
+ *   z = (Cast(MatMulInteger(q, W, a_zp, b_zp)) * (a_scale * w_scale) + bias)
+ *       + residual                                  (as icx_quant_linear)
+ *   out = LayerNormalization(z, gamma, beta, epsilon) over the last axis
+ * Replaces the reference's MatMulInteger -> Cast -> Mul -> Add -> Add ->
+ * LayerNormalization chain of one transformer sub-block
+ * (src/operators/layer_normalization.rs:25-80 for the last step; the
+ * normalisation sums in a different order, fp32 rounding).  z is never
+ * written.  N must be 192 x 2..4 and K a multiple of 16 (else
+ * ICX_ERR_INVALID); all operands 16-byte aligned.  d_minmax receives one
+ * (min, max) pair of `out` per CTA (*n_minmax of them), like
+ * icx_quant_linear.
+ * ======================================================================== */
+ICX_API int icx_quant_linear_layernorm(void* stream, const uint8_t* d_q, const float* d_a_scale,
+                                       const uint8_t* d_a_zp, const int32_t* d_rowsum_q,
+                                       const int8_t* d_wt, const int32_t* d_colsum, size_t M,
+                                       size_t K, size_t N, const float* d_w_scale,
+                                       int w_scale_per_col, const int8_t* d_b_zp, int b_zp_per_col,
+                                       const float* d_bias, const float* d_residual,
+                                       const float* d_gamma, const float* d_beta, float epsilon,
+                                       float* d_out, float* d_minmax, int* n_minmax);
+
+/* ======================================================================== *
  * DequantizeLinear: y = (f32(x) - f32(zp)) * scale, per tensor or per axis.
  * Replaces gpu_dequantize_linear (src/cuda/ops/quantize.rs:24-267) and
  * dequantize_linear_{i8,u8,i32}_kernel (src/cuda/ops/quantize_kernels.rs:

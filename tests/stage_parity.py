@@ -15,6 +15,8 @@ oracle restatement of the reference operators:
   Mul, Add and the residual Add each rounded as the reference's CPU
   GraphExecutor does (graph_executor.rs:92-278);
 * QuantLinear+GELU: within the GELU tolerance (1e-5 absolute);
+* QuantLinear+Residual+LayerNorm: the oracle's exact residual sum put
+  through the restated LayerNormalization, within 4e-6 absolute;
 * LayerNormalization: on sampled rows against the restated reference
   operator (layer_normalization.rs:25-80) within 4e-6 absolute (the kernel
   sums with a warp tree and multiplies by rsqrt instead of dividing by
@@ -93,7 +95,15 @@ def check_plan(ex, inits: dict, rows: int = 64, threads: int = 8, attrs: dict | 
             ref = np.concatenate(parts, axis=1)
             if res is not None:
                 ref = np.add(ref, res.reshape(-1, res.shape[-1])[r], dtype=np.float32)
-            if gelu:
+            if info.get("ln_gamma"):
+                # the residual sum is exact; its LayerNorm within LN_ATOL
+                ref = oracle.layer_normalization(
+                    ref, inits[info["ln_gamma"]],
+                    inits[info["ln_beta"]] if info["ln_beta"] else None, float(info["ln_eps"]))
+                err = np.abs(got.astype(np.float64) - ref).max()
+                assert err <= LN_ATOL, f"step {i} {op} {node}: LayerNorm output off by {err}"
+                counts["layernorm"] = counts.get("layernorm", 0) + 1
+            elif gelu:
                 err = np.abs(got - ref).max()
                 assert err <= GELU_ATOL, f"step {i} {op} {node}: GELU output off by {err}"
             elif not np.array_equal(got.view(np.uint32), ref.view(np.uint32)):

@@ -393,3 +393,56 @@ def test_s32_matmul_integer_cta_pairs_bit_exact():
     bz = rng.integers(-8, 9, (N,)).astype(np.int8)
     got = host(ops.gpu_matmul_integer(cu(a), cu(b), cu(az), cu(bz)))
     np.testing.assert_array_equal(got, oracle.matmul_integer(a, b, az, bz, threads=8))
+
+
+# QuantLinear + residual Add + LayerNormalization in one launch: clusters of
+# N / 192 CTAs hold whole rows and exchange the row statistics through
+# distributed shared memory.  The residual sum before the LayerNorm is exact
+# (the QuantLinear epilogue's arithmetic); the normalisation sums in another
+# order than the reference (layer_normalization.rs:25-80), so y is compared
+# with the restated operator within the LayerNorm kernel's 4e-6.
+@pytest.mark.parametrize("M,K,N,per_col,beta", [
+    (4096, 768, 768, False, True),      # DistilBERT O-proj
+    (4096, 3072, 768, False, True),     # DistilBERT FFN2 (deep ring)
+    (1000, 768, 768, True, True),       # per-column scale / zero point, ragged M
+    (300, 768, 384, False, False),      # clusters of two, no beta
+    (77, 1536, 576, True, True),        # clusters of three, deep
+])
+def test_quant_linear_layernorm(M, K, N, per_col, beta):
+    x = synth.normal((M, K), 1.0, 51)
+    w = synth.int8_uniform((K, N), 52)
+    bias = synth.normal((N,), 0.02, 53)
+    if per_col:
+        ws = synth.uniform_f32((N,), 0.005, 0.02, 54)
+        bz = synth.int8_uniform((N,), 55, -8, 8)
+    else:
+        ws, bz = np.array([0.01], np.float32), None
+    res = synth.normal((M, N), 1.0, 56)
+    gamma = (1.0 + synth.normal((N,), 0.05, 57)).astype(np.float32)
+    bet = synth.normal((N,), 0.05, 58) if beta else None
+    pw = ops.prepare_weight(cu(w))
+    outs = ops.gpu_dynamic_quantize_linear(cu(x), row_len=K if bz is not None else None)
+    y, s, z = outs[:3]
+    rows = outs[3] if bz is not None else None
+    mm = ops.MinMaxPartials(DEV)
+    out = ops.quant_linear_layernorm(y, s, z, pw, cu(ws), cu(res), cu(gamma),
+                                     None if bet is None else cu(bet), 1e-5, cu(bias),
+                                     None if bz is None else cu(bz), rows, minmax=mm)
+    zsum = oracle.quant_linear_from_q(host(y), host(s).item(), host(z).item(), w, ws, bias, bz,
+                                      residual=res, threads=8)
+    ref = oracle.layer_normalization(zsum, gamma, bet, 1e-5)
+    got = host(out)
+    assert np.abs(got.astype(np.float64) - ref).max() <= 4e-6
+    # the (min, max) partials cover exactly the output (seeded with 0)
+    parts = host(mm.buf)[:mm.n]
+    assert mm.n >= N // 192
+    assert parts[:, 0].min() == min(0.0, got.min()) and parts[:, 1].max() == max(0.0, got.max())
+
+
+def test_quant_linear_layernorm_rejects_unsupported_widths():
+    x = cu(np.zeros((4, 64), np.uint8))
+    pw = ops.prepare_weight(cu(synth.int8_uniform((64, 200), 1)))
+    one = cu(np.array(1.0, np.float32))
+    with pytest.raises(IcxError, match="unsupported"):
+        ops.quant_linear_layernorm(x, one, cu(np.array(0, np.uint8)), pw, cu(np.array([0.01], np.float32)),
+                                   cu(np.zeros((4, 200), np.float32)), cu(np.ones(200, np.float32)))
