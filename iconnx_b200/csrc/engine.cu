@@ -1173,7 +1173,7 @@ class Engine {
         if (g && L.in[0] == cur && g->dtype == ICX_F32 && numel(g->shape) == N &&
             (L.in.size() <= 2 || L.in[2].empty() || (b && b->dtype == ICX_F32 && numel(b->shape) == N)) &&
             (axis == -1 || axis == rank - 1) && only_y &&
-            quant_linear_ln_supported((size_t)w->shape[0], (size_t)N)) {
+            quant_linear_ln_preferred((size_t)(numel(vals_[cur].shape) / N), (size_t)w->shape[0], (size_t)N)) {
           f.ln_gamma = L.in[1];
           f.ln_beta = L.in.size() > 2 ? L.in[2] : std::string();
           f.ln_eps = L.getf("epsilon", 1e-5f);

@@ -24,6 +24,9 @@ int layernorm_partials(size_t rows);
 // Whether icx_quant_linear_layernorm runs for this K and N on the current
 // device (qgemm.cu).
 bool quant_linear_ln_supported(size_t K, size_t N);
+// ... and whether the engine prefers it to the unfused GEMM + LayerNorm
+// (where every 128-row block gets a cluster of its own).
+bool quant_linear_ln_preferred(size_t M, size_t K, size_t N);
 
 int launch_layernorm(cudaStream_t s, const float* x, const float* gamma, const float* beta,
                      float* y, size_t rows, size_t D, float eps, float* minmax, int* n_minmax);

@@ -1621,7 +1621,22 @@ static int max_ln_clusters(int ncl) {
 
 namespace icx {
 bool quant_linear_ln_supported(size_t K, size_t N);
+bool quant_linear_ln_preferred(size_t M, size_t K, size_t N);
 }  // namespace icx
+
+// Whether the engine should fuse the LayerNorm into the GEMM: where every
+// 128-row block gets a cluster of its own (one tile per CTA), so that the
+// longer epilogue only adds latency.  With several tiles per CTA the
+// epilogue's throughput sets the pace and the unfused GEMM (CTA pairs at
+// deep K) plus a separate LayerNorm was measured faster (BERT-base config 4,
+// M = 32768: 3926 against 3853 seq/s).
+bool icx::quant_linear_ln_preferred(size_t M, size_t K, size_t N) {
+  if (!quant_linear_ln_supported(K, N)) return false;
+  const int ncl = (int)(N / 192);
+  const size_t num_m = (M + kBM - 1) / kBM;
+  const int cl = K >= 1536 ? max_ln_clusters<true>(ncl) : max_ln_clusters<false>(ncl);
+  return num_m <= (size_t)cl;
+}
 
 bool icx::quant_linear_ln_supported(size_t K, size_t N) {
   if (K == 0 || K % 16 != 0 || K >= (1u << 30) || N % 192 != 0) return false;
