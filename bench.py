@@ -592,12 +592,13 @@ def run_kernel_probe(args):
     from iconnx_b200 import graphs, ops, synth
     dev = torch.device("cuda", 0)
     M, K, N = [int(v) for v in args.shape.split(",")]
-    if args.kernel in ("ffn1", "gemm", "gemm_pc", "quant", "residual"):
+    if args.kernel in ("ffn1", "gemm", "gemm_pc", "quant", "residual", "residual_ln"):
         x = torch.from_numpy(synth.normal((M, K), 1.0, 0)).to(dev)
         w = ops.prepare_weight(torch.from_numpy(synth.int8_uniform((K, N), 1)).to(dev))
         b = torch.from_numpy(synth.normal((N,), 0.02, 2)).to(dev)
         ws = torch.tensor([0.01], dtype=torch.float32, device=dev)
-        res = torch.from_numpy(synth.normal((M, N), 1.0, 5)).to(dev) if args.kernel == "residual" else None
+        res = (torch.from_numpy(synth.normal((M, N), 1.0, 5)).to(dev)
+               if args.kernel in ("residual", "residual_ln") else None)
         bz = rows = None
         if args.kernel == "gemm_pc":
             # config 4's per-column weight scale and int8 zero point
@@ -608,7 +609,12 @@ def run_kernel_probe(args):
             y, s, z = ops.gpu_dynamic_quantize_linear(x)
         out = torch.empty((M, N), dtype=torch.float32, device=dev)
         mm = ops.MinMaxPartials(dev)
-        for _ in range(3):
+        if args.kernel == "residual_ln":
+            gamma = torch.from_numpy(synth.normal((N,), 1.0, 6)).to(dev)
+            beta = torch.from_numpy(synth.normal((N,), 0.02, 7)).to(dev)
+            for _ in range(3):
+                ops.quant_linear_layernorm(y, s, z, w, ws, res, gamma, beta, bias=b, out=out, minmax=mm)
+        for _ in range(3 if args.kernel != "residual_ln" else 0):
             ops.quant_linear(y, s, z, w, ws, b, bz, rows, gelu=args.kernel == "ffn1", out=out,
                              minmax=mm if args.kernel == "quant" else None, residual=res)
             if args.kernel == "quant":
@@ -715,7 +721,8 @@ def main():
     ap.add_argument("--scaling", default="weak", choices=["weak", "strong"],
                     help="weak: every GPU runs the config's batch; strong (encoders): the "
                          "config's batch is split across the GPUs")
-    ap.add_argument("--kernel", choices=["ffn1", "gemm", "gemm_pc", "quant", "residual", "attention"],
+    ap.add_argument("--kernel", choices=["ffn1", "gemm", "gemm_pc", "quant", "residual", "residual_ln",
+                                                 "attention"],
                     help="launch one kernel of the path a few times and exit (ncu captures)")
     ap.add_argument("--shape", default="4096,768,3072",
                     help="M,K,N for --kernel (attention: batch,seq,0)")
